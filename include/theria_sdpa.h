@@ -1,0 +1,135 @@
+/*
+ * theria_sdpa.h -- C ABI of the B200 (sm_100a) higher-order SDPA library
+ * (libtheria_sm100.so).
+ *
+ * Every entry point takes raw device pointers to contiguous row-major
+ * tensors, plain sizes, and a cudaStream_t passed as void*.  Layouts:
+ *   q, tq, dout, w, o, o_tan, dq, hq       [B, H, T, D]
+ *   k, v, tk, tv, dk, dv, hk, hv           [B, H, M, D]
+ *   lse                                    [B, H, T]  float32
+ * D == Dv.  All input tensors of one call share `dtype`.  Nothing here
+ * allocates device memory: outputs and the workspace are the caller's.
+ * Calls are stream-ordered and asynchronous (no host synchronisation) and
+ * keep no mutable global state.  Each returns a THERIA_* status.
+ *
+ * Causal masking is top-left aligned: query row i attends to keys j <= i.
+ *
+ * The reference library (alexgabel/theria) has no native layer; the entry
+ * points replace its Python/Triton operator functions, cited per function
+ * (paths inside the theria project).
+ */
+#ifndef THERIA_SDPA_H
+#define THERIA_SDPA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define THERIA_OK 0
+#define THERIA_ERR_INVALID_ARG 1  /* null pointer, bad size, bad dtype   */
+#define THERIA_ERR_UNSUPPORTED 2  /* head_dim or shape out of range      */
+#define THERIA_ERR_LAUNCH 3       /* a CUDA launch returned an error     */
+#define THERIA_ERR_WORKSPACE 4    /* workspace missing or too small      */
+#define THERIA_ERR_DEVICE_TIMEOUT 5 /* a device-side wait gave up        */
+
+/* element types */
+#define THERIA_F32 0
+#define THERIA_F16 1
+#define THERIA_BF16 2
+
+/* largest head dimension any entry point accepts */
+#define THERIA_MAX_HEAD_DIM 128
+
+/* Human-readable text for a status code (static string, never NULL). */
+const char* theria_status_string(int status);
+
+/* Library version, e.g. "theria-sm100 0.1.0". */
+const char* theria_version(void);
+
+/*
+ * Forward: o = softmax(scale * q k^T [+ causal mask]) v, and the row
+ * logsumexp lse = m + log(l) of the scaled scores.
+ * `o_dtype` is THERIA_F32 or `dtype` (the reference's fused forward returns
+ * float32; its public sdpa_custom returns q.dtype).  `lse` may be NULL.
+ * Replaces triton_sdpa_fused / _fused_sdpa_kernel
+ * (theria/attention/triton_qk.py:242-369).
+ */
+int theria_sdpa_fwd(const void* q, const void* k, const void* v,
+                    void* o, int o_dtype, float* lse,
+                    int64_t B, int64_t H, int64_t T, int64_t M, int64_t D,
+                    int dtype, float scale, int causal, void* stream);
+
+/* Bytes of workspace theria_sdpa_bwd / theria_sdpa_hvp need. */
+int64_t theria_sdpa_bwd_workspace_bytes(int64_t B, int64_t H, int64_t T,
+                                        int64_t M, int64_t D);
+int64_t theria_sdpa_hvp_workspace_bytes(int64_t B, int64_t H, int64_t T,
+                                        int64_t M, int64_t D);
+
+/*
+ * Backward: dq, dk, dv of <o, dout> from the saved lse.
+ * `o` (the forward output, dtype `o_dtype`) may be NULL, in which case the
+ * row term z = rowsum(dout * o) is rebuilt from lse.  Any of dq/dk/dv may be
+ * NULL to skip storing it.  Outputs have `dtype`.
+ * Replaces sdpa_bwd_dq / sdpa_bwd_dk / sdpa_bwd_dv
+ * (theria/attention/triton_sdpa_backward.py:505-696, :269-462, :106-266)
+ * and the backward of TritonFusedSDPAFunction (triton_qk.py:379-387).
+ */
+int theria_sdpa_bwd(const void* q, const void* k, const void* v,
+                    const void* o, int o_dtype, const void* dout,
+                    const float* lse, void* dq, void* dk, void* dv,
+                    void* workspace, int64_t workspace_bytes,
+                    int64_t B, int64_t H, int64_t T, int64_t M, int64_t D,
+                    int dtype, float scale, int causal, void* stream);
+
+/*
+ * Frozen-stats JVP: o_tan = Pdot v + P tv with P rebuilt from lse and
+ * Pdot = P * (Sdot - rowsum(P * Sdot)), Sdot = scale (tq k^T + q tk^T).
+ * At the saved point this is the exact tangent of o.
+ * Replaces sdpa_jvp (theria/attention/triton_sdpa_backward.py:465-503).
+ */
+int theria_sdpa_jvp(const void* q, const void* k, const void* v,
+                    const void* tq, const void* tk, const void* tv,
+                    const float* lse, void* o_tan,
+                    int64_t B, int64_t H, int64_t T, int64_t M, int64_t D,
+                    int dtype, float scale, int causal, void* stream);
+
+/*
+ * Hessian-vector product of L = <o, w> along u = (tq, tk, tv):
+ *   hq, hk, hv = d/de grad_{q,k,v} L(q + e tq, k + e tk, v + e tv) at e = 0
+ * and o_tan = J u (the derivative of <grad L, u> with respect to w).
+ * This is the double-backward of the attention backward.  Any output may
+ * be NULL to skip storing it.
+ * Replaces hvp_fd_vjp (theria/attention/hvp_utils.py:30-49), sdpa_hvp
+ * (theria/attention/reference_hvp_sdpa.py:46-97) and the
+ * create_graph=True backward of SDPACustom
+ * (theria/autograd/sdpa_custom_function.py:31-53).
+ */
+int theria_sdpa_hvp(const void* q, const void* k, const void* v,
+                    const void* w, const float* lse,
+                    const void* tq, const void* tk, const void* tv,
+                    void* hq, void* hk, void* hv, void* o_tan,
+                    void* workspace, int64_t workspace_bytes,
+                    int64_t B, int64_t H, int64_t T, int64_t M, int64_t D,
+                    int dtype, float scale, int causal, void* stream);
+
+/* Number of kernels this library has launched in this process (all devices,
+ * all threads); for accounting in benchmarks and tests. */
+int64_t theria_launch_count(void);
+
+/*
+ * Device-side error word of the current device: non-zero once a kernel's
+ * bounded wait gave up (THERIA_ERR_DEVICE_TIMEOUT).  Reading it synchronises
+ * `stream`.  theria_clear_device_error resets it (stream-ordered).
+ */
+int theria_get_device_error(int* out_flag, void* stream);
+int theria_clear_device_error(void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* THERIA_SDPA_H */

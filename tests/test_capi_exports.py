@@ -1,0 +1,86 @@
+"""The C-ABI library loads and exports every entry point include/theria_sdpa.h
+declares; host-only calls (status strings, workspace sizes, argument
+rejection) behave.  No kernel is launched, so no GPU is needed."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from theria_b200 import _lib
+
+HEADER = os.path.join(os.path.dirname(__file__), "..", "include", "theria_sdpa.h")
+
+
+def declared_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(theria_\w+)\s*\(", src)))
+
+
+def test_header_declares_the_entry_points():
+    names = declared_functions()
+    for n in ("theria_sdpa_fwd", "theria_sdpa_bwd", "theria_sdpa_jvp", "theria_sdpa_hvp"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+
+
+def test_binding_covers_every_declared_symbol():
+    assert set(declared_functions()) == set(_lib.SIGNATURES)
+
+
+def test_status_strings_and_version():
+    lib = _lib.load()
+    assert lib.theria_version().decode().startswith("theria-sm100")
+    for code in range(6):
+        assert lib.theria_status_string(code)
+    assert lib.theria_status_string(0).decode() == "ok"
+
+
+def test_workspace_sizes():
+    lib = _lib.load()
+    b = lib.theria_sdpa_bwd_workspace_bytes(4, 16, 4096, 4096, 128)
+    assert b >= 4 * 16 * 4096 * 4 and b % 256 == 0
+    h = lib.theria_sdpa_hvp_workspace_bytes(2, 8, 2048, 2048, 64)
+    assert h >= 3 * 2 * 8 * 2048 * 4 and h % 256 == 0
+
+
+@pytest.mark.parametrize("bad", [
+    dict(D=0), dict(D=129), dict(dtype=7), dict(T=-1), dict(B=70000, H=1), dict(M=0),
+])
+def test_fwd_rejects_bad_arguments_before_touching_the_device(bad):
+    lib = _lib.load()
+    a = dict(B=1, H=1, T=4, M=4, D=16, dtype=0)
+    a.update(bad)
+    p = ctypes.c_void_p(16)  # never dereferenced: validation fails first
+    st = lib.theria_sdpa_fwd(p, p, p, p, 0, None, a["B"], a["H"], a["T"], a["M"], a["D"],
+                             a["dtype"], 0.25, 0, None)
+    assert st in (_lib.THERIA_ERR_INVALID_ARG, _lib.THERIA_ERR_UNSUPPORTED)
+
+
+def test_null_pointers_rejected():
+    lib = _lib.load()
+    st = lib.theria_sdpa_jvp(None, None, None, None, None, None, None, None,
+                             1, 1, 4, 4, 16, 0, 0.25, 0, None)
+    assert st == _lib.THERIA_ERR_INVALID_ARG
+
+
+def test_bwd_without_workspace_rejected():
+    lib = _lib.load()
+    p = ctypes.c_void_p(16)
+    st = lib.theria_sdpa_bwd(p, p, p, None, 0, p, p, p, p, p, None, 0,
+                             1, 1, 4, 4, 16, 0, 0.25, 0, None)
+    assert st == _lib.THERIA_ERR_WORKSPACE
+
+
+def test_empty_problem_is_a_no_op():
+    lib = _lib.load()
+    st = lib.theria_sdpa_fwd(None, None, None, None, 0, None, 0, 4, 4, 4, 16, 0, 0.25, 0,
+                             None)
+    assert st == _lib.THERIA_OK

@@ -1,0 +1,137 @@
+"""Parity of the CUDA kernels with the CPU oracle (and with the reference's
+own golden vectors), through the tensor-level operators over the C ABI.
+
+Tolerances (the contract): fp32 max relative error (max|x-ref| / max|ref|)
+<= 1e-5 for O, dQ, dK, dV and the JVP, <= 1e-4 for the HVP; bf16/fp16 max
+absolute error <= 2e-2 against the fp32 oracle on the same (rounded) inputs.
+"""
+
+import pytest
+import torch
+
+from oracle import sdpa_oracle as orc
+from tests._util import load_golden, max_abs, max_rel
+
+pytestmark = pytest.mark.gpu
+
+cuda = pytest.importorskip("torch").cuda
+if not cuda.is_available():
+    pytest.skip("CUDA not available", allow_module_level=True)
+
+from theria_b200.attention import ops  # noqa: E402
+
+DEV = "cuda"
+TOL_REL = 1e-5
+TOL_REL_HVP = 1e-4
+TOL_ABS_LP = 2e-2
+
+
+def _draw(shape_q, shape_k, dtype, seed=0, n_q=4, n_k=5):
+    g = torch.Generator("cpu").manual_seed(seed)
+    qs = [torch.randn(*shape_q, generator=g).to(dtype) for _ in range(n_q)]
+    ks = [torch.randn(*shape_k, generator=g).to(dtype) for _ in range(n_k)]
+    return qs, ks
+
+
+def _check(x, ref, dtype, hvp=False):
+    if dtype == torch.float32:
+        tol = TOL_REL_HVP if hvp else TOL_REL
+        err = max_rel(x, ref)
+        assert err <= tol, f"max rel err {err:.3e} > {tol}"
+    else:
+        err = max_abs(x, ref)
+        assert err <= TOL_ABS_LP, f"max abs err {err:.3e} > {TOL_ABS_LP}"
+
+
+@pytest.mark.parametrize("case", ["cfg1", "maml"])
+def test_kernels_match_reference_golden_vectors(case):
+    g = load_golden(case)
+    d = {k: v.to(DEV) for k, v in g.items() if k.startswith("in_")}
+    q, k, v = d["in_q"], d["in_k"], d["in_v"]
+    o, lse = ops.forward(q, k, v)
+    assert max_rel(o, g["out_o"]) <= TOL_REL
+    dq, dk, dv = ops.backward(q, k, v, d["in_dout"], lse, o=o)
+    for x, n in zip((dq, dk, dv), ("dq", "dk", "dv")):
+        assert max_rel(x, g[f"out_{n}"]) <= TOL_REL, n
+    t = ops.jvp(q, k, v, d["in_tq"], d["in_tk"], d["in_tv"], lse)
+    assert max_rel(t, g["out_jvp"]) <= TOL_REL
+    hq, hk, hv, _ = ops.hvp(q, k, v, d["in_dout"], lse, d["in_vq"], d["in_vk"], d["in_vv"])
+    for x, n in zip((hq, hk, hv), ("q", "k", "v")):
+        assert max_rel(x, g[f"out_hvp_w_{n}"]) <= TOL_REL_HVP, n
+    ones = torch.ones_like(q)
+    hq, hk, hv, _ = ops.hvp(q, k, v, ones, lse, d["in_vq"], d["in_vk"], d["in_vv"])
+    for x, n in zip((hq, hk, hv), ("q", "k", "v")):
+        assert max_rel(x, g[f"out_hvp_sum_{n}"]) <= TOL_REL_HVP, n
+
+
+SHAPES = [
+    # (B, H, T, M, D)
+    (1, 1, 1, 1, 32),      # single row (the reference's T=1 regression)
+    (1, 2, 33, 33, 16),    # ragged tile edge, MAML head dim
+    (2, 2, 64, 64, 32),    # cfg1
+    (1, 2, 40, 70, 32),    # T != M
+    (1, 2, 130, 130, 64),
+    (1, 1, 257, 257, 128),
+    (1, 1, 200, 200, 48),  # head dim off the tensor-core list
+]
+DTYPES = [torch.float32, torch.bfloat16, torch.float16]
+
+
+def _ids(s):
+    return "x".join(map(str, s))
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=_ids)
+@pytest.mark.parametrize("dtype", DTYPES, ids=str)
+@pytest.mark.parametrize("causal", [False, True])
+def test_forward_and_backward_match_oracle(shape, dtype, causal):
+    B, H, T, M, D = shape
+    (q, do, _, _), (k, v, _, _, _) = _draw((B, H, T, D), (B, H, M, D), dtype)
+    o, lse = ops.forward(q.to(DEV), k.to(DEV), v.to(DEV), causal=causal)
+    qf, kf, vf, dof = q.float(), k.float(), v.float(), do.float()
+    _check(o, orc.attention(qf, kf, vf, causal=causal), dtype)
+    _, _, lse_ref = orc.row_stats(qf, kf, causal=causal)
+    assert max_abs(lse, lse_ref) <= 1e-4 * max(1.0, lse_ref.abs().max().item())
+    for with_o in (True, False):
+        dq, dk, dv = ops.backward(q.to(DEV), k.to(DEV), v.to(DEV), do.to(DEV), lse,
+                                  o=o if with_o else None, causal=causal)
+        for x, r in zip((dq, dk, dv), orc.backward(qf, kf, vf, dof, causal=causal)):
+            _check(x, r, dtype)
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=_ids)
+@pytest.mark.parametrize("dtype", DTYPES, ids=str)
+@pytest.mark.parametrize("causal", [False, True])
+def test_jvp_and_hvp_match_oracle(shape, dtype, causal):
+    B, H, T, M, D = shape
+    (q, w, tq, _), (k, v, tk, tv, _) = _draw((B, H, T, D), (B, H, M, D), dtype, seed=1)
+    qd, kd, vd = q.to(DEV), k.to(DEV), v.to(DEV)
+    _, lse = ops.forward(qd, kd, vd, causal=causal)
+    f = [t.float() for t in (q, k, v, w, tq, tk, tv)]
+    ot = ops.jvp(qd, kd, vd, tq.to(DEV), tk.to(DEV), tv.to(DEV), lse, causal=causal)
+    _check(ot, orc.jvp(f[0], f[1], f[2], f[4], f[5], f[6], causal=causal), dtype)
+    hq, hk, hv, ot2 = ops.hvp(qd, kd, vd, w.to(DEV), lse, tq.to(DEV), tk.to(DEV), tv.to(DEV),
+                              causal=causal)
+    ref = orc.hvp(*f, causal=causal)
+    for x, r in zip((hq, hk, hv, ot2), ref):
+        _check(x, r, dtype, hvp=True)
+
+
+def test_outputs_can_be_skipped():
+    (q, do, _, _), (k, v, _, _, _) = _draw((1, 2, 48, 32), (1, 2, 48, 32), torch.float32)
+    q, do, k, v = (t.to(DEV) for t in (q, do, k, v))
+    _, lse = ops.forward(q, k, v)
+    dq, dk, dv = ops.backward(q, k, v, do, lse, need=(False, True, False))
+    assert dq is None and dv is None
+    ref = orc.backward(q.cpu(), k.cpu(), v.cpu(), do.cpu())
+    assert max_rel(dk, ref[1]) <= TOL_REL
+
+
+def test_device_error_word_is_clear():
+    import ctypes
+    from theria_b200 import _lib
+    lib = _lib.load()
+    flag = ctypes.c_int(-1)
+    s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    assert lib.theria_get_device_error(ctypes.byref(flag), s) == 0
+    assert flag.value == 0

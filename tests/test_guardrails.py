@@ -1,0 +1,53 @@
+"""Loud host-side validation with the reference's messages (no GPU needed:
+every check fires before a kernel is launched)."""
+
+import pytest
+import torch
+
+from theria_b200.attention import (sdpa_bwd_dq, sdpa_bwd_dk, sdpa_bwd_dv, sdpa_jvp,
+                                   triton_sdpa_fused)
+from theria_b200.attention.custom import sdpa_custom
+from theria_b200.attention import ops
+
+
+def _cpu(shape=(1, 1, 4, 8)):
+    return [torch.randn(*shape) for _ in range(3)]
+
+
+def test_backward_requires_cuda():
+    q, k, v = _cpu()
+    m = torch.zeros(1, 1, 4)
+    with pytest.raises(AssertionError, match="requires CUDA"):
+        sdpa_bwd_dq(q, k, v, q, m, m + 1, 0.3)
+    with pytest.raises(AssertionError, match="requires CUDA"):
+        sdpa_bwd_dk(q, k, v, q, m, m + 1, 0.3)
+    with pytest.raises(AssertionError, match="requires CUDA"):
+        sdpa_bwd_dv(q, k, q, m, m + 1, 0.3)
+
+
+def test_jvp_requires_cuda():
+    q, k, v = _cpu()
+    m = torch.zeros(1, 1, 4)
+    with pytest.raises(AssertionError, match="requires CUDA"):
+        sdpa_jvp(q, k, v, q, k, v, m, m + 1, 0.3)
+
+
+def test_forward_requires_cuda():
+    q, k, v = _cpu()
+    with pytest.raises(AssertionError):
+        triton_sdpa_fused(q, k, v)
+    with pytest.raises(AssertionError, match="requires CUDA"):
+        ops.forward(q, k, v)
+
+
+def test_unknown_backend_is_rejected_not_rerouted():
+    q, k, v = _cpu()
+    for name in ("reference", "triton_qk", "triton_fast", "bogus"):
+        with pytest.raises(ValueError, match="Unsupported sdpa_custom backend"):
+            sdpa_custom(q, k, v, backend=name)
+
+
+def test_no_cpu_fallback_for_fused_backend():
+    q, k, v = _cpu()
+    with pytest.raises(AssertionError, match="requires CUDA"):
+        sdpa_custom(q, k, v, backend="triton_full_fused")

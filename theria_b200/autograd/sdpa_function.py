@@ -1,0 +1,16 @@
+"""``theria.autograd.sdpa_function`` surface (reference file :1-44).
+
+In the reference ``SDPAFunction`` is the documented *failing* boundary
+(autograd-in-backward without create_graph).  Here the name resolves to the
+twice-differentiable fused function, so ``sdpa`` supports grad-of-grad.
+"""
+
+from theria_b200.attention.fused import SDPAFunction
+
+
+def sdpa(q, k, v, causal: bool = False):
+    """Public SDPA entry point: inputs (B, H, T, D), output (B, H, T, D)."""
+    return SDPAFunction.apply(q, k, v, causal, None)
+
+
+__all__ = ["SDPAFunction", "sdpa"]

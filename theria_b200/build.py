@@ -1,0 +1,75 @@
+"""Build libtheria_sm100.so in-tree with nvcc (sm_100a only).
+
+    python -m theria_b200.build [--verbose]
+
+The library is one translation unit (csrc/theria_sm100.cu) compiled for
+``arch=compute_100a,code=sm_100a``; nvcc cross-compiles it on a machine
+without a GPU.  The output lands next to this file so it travels with the
+source tree.
+"""
+
+from __future__ import annotations
+
+import argparse
+import os
+import shutil
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+CSRC = os.path.join(HERE, "csrc")
+LIB = os.path.join(HERE, "libtheria_sm100.so")
+ROOT = os.path.dirname(HERE)
+
+NVCC_FLAGS = [
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-O3", "-lineinfo", "-std=c++17",
+    "-shared", "-Xcompiler", "-fPIC",
+    "--expt-relaxed-constexpr",
+]
+
+
+def _nvcc():
+    for cand in (shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if cand and os.path.exists(cand):
+            return cand
+    raise RuntimeError("nvcc not found: cannot build libtheria_sm100.so")
+
+
+def sources():
+    return sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC)
+                  if f.endswith((".cu", ".cuh")))
+
+
+def up_to_date():
+    if not os.path.exists(LIB):
+        return False
+    t = os.path.getmtime(LIB)
+    deps = sources() + [os.path.join(ROOT, "include", "theria_sdpa.h"), __file__]
+    return all(os.path.getmtime(p) <= t for p in deps if os.path.exists(p))
+
+
+def build(force: bool = False, verbose: bool = False, extra=()) -> str:
+    if not force and up_to_date():
+        return LIB
+    cmd = [_nvcc(), *NVCC_FLAGS, *extra, "-I", os.path.join(ROOT, "include"),
+           os.path.join(CSRC, "theria_sm100.cu"), "-o", LIB + ".tmp", "-lcuda"]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    subprocess.run(cmd, check=True)
+    os.replace(LIB + ".tmp", LIB)
+    return LIB
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--force", action="store_true")
+    ap.add_argument("--verbose", action="store_true")
+    ap.add_argument("--ptxas-v", action="store_true", help="print register/smem use")
+    a = ap.parse_args()
+    extra = ["-Xptxas", "-v"] if a.ptxas_v else []
+    print(build(force=a.force or a.ptxas_v, verbose=a.verbose, extra=extra))
+
+
+if __name__ == "__main__":
+    sys.exit(main())

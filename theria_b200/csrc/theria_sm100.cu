@@ -1,0 +1,250 @@
+// libtheria_sm100.so: the C ABI declared in include/theria_sdpa.h.
+//
+// The whole library is one translation unit (no relocatable device code):
+// this file includes the kernel headers and implements argument checking,
+// workspace carving and kernel selection for each entry point.
+#include <cstdio>
+
+#include "common.cuh"
+#include "sdpa_simt.cuh"
+
+namespace theria {
+namespace {
+
+constexpr int64_t kAlign = 256;
+
+int64_t align_up(int64_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
+
+bool valid_dtype(int dt) { return dt == THERIA_F32 || dt == THERIA_F16 || dt == THERIA_BF16; }
+
+// Shared argument checks; returns THERIA_OK or an error status.
+int check_shape(int64_t B, int64_t H, int64_t T, int64_t M, int64_t D, int dtype) {
+  if (B < 0 || H < 0 || T < 0 || M < 0 || D <= 0) return THERIA_ERR_INVALID_ARG;
+  if (!valid_dtype(dtype)) return THERIA_ERR_INVALID_ARG;
+  if (D > THERIA_MAX_HEAD_DIM) return THERIA_ERR_UNSUPPORTED;
+  if (B * H > 65535) return THERIA_ERR_UNSUPPORTED;  // grid.y carries batch*head
+  if (M == 0 && T > 0) return THERIA_ERR_INVALID_ARG; // softmax over no keys
+  return THERIA_OK;
+}
+
+bool empty_problem(int64_t B, int64_t H, int64_t T) { return B == 0 || H == 0 || T == 0; }
+
+template <typename K>
+void set_smem(K kernel, size_t bytes) {
+  if (bytes > 48 * 1024)
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+}
+
+size_t tile_floats(int64_t D) { return (size_t)simt::KT * (D + 1); }
+
+dim3 row_grid(const Shape& s) {
+  return dim3((unsigned)((s.T + simt::WARPS - 1) / simt::WARPS), (unsigned)(s.B * s.H));
+}
+dim3 col_grid(const Shape& s) {
+  return dim3((unsigned)((s.M + simt::WARPS - 1) / simt::WARPS), (unsigned)(s.B * s.H));
+}
+
+// ------------------------------------------------------------- SIMT launches
+template <typename T>
+int simt_fwd(const void* q, const void* k, const void* v, void* o, int o_dtype, float* lse,
+             const Shape& s, cudaStream_t st) {
+  size_t sm = (2 * tile_floats(s.D) + simt::WARPS * s.D) * sizeof(float);
+  auto kern = simt::fwd_row_kernel<T>;
+  set_smem(kern, sm);
+  kern<<<row_grid(s), simt::WARPS * 32, sm, st>>>((const T*)q, (const T*)k, (const T*)v, o,
+                                                  o_dtype, lse, s);
+  return launch_status();
+}
+
+template <typename T>
+int simt_bwd(const void* q, const void* k, const void* v, const void* o, int o_dtype,
+             const void* dout, const float* lse, void* dq, void* dk, void* dv, float* z,
+             const Shape& s, cudaStream_t st) {
+  const int64_t rows = s.B * s.H * s.T;
+  if (o != nullptr) {
+    simt::delta_from_o_kernel<T><<<(unsigned)((rows + simt::WARPS - 1) / simt::WARPS),
+                                   simt::WARPS * 32, 0, st>>>(o, o_dtype, (const T*)dout, z,
+                                                              rows, (int)s.D);
+  } else {
+    size_t sm = (2 * tile_floats(s.D) + simt::WARPS * 2 * s.D) * sizeof(float);
+    auto kern = simt::delta_from_stats_kernel<T>;
+    set_smem(kern, sm);
+    kern<<<row_grid(s), simt::WARPS * 32, sm, st>>>((const T*)q, (const T*)k, (const T*)v,
+                                                    (const T*)dout, lse, z, s);
+  }
+  if (int e = launch_status()) return e;
+  if (dq != nullptr) {
+    size_t sm = (2 * tile_floats(s.D) + simt::WARPS * 2 * s.D) * sizeof(float);
+    auto kern = simt::dq_row_kernel<T>;
+    set_smem(kern, sm);
+    kern<<<row_grid(s), simt::WARPS * 32, sm, st>>>((const T*)q, (const T*)k, (const T*)v,
+                                                    (const T*)dout, lse, z, (T*)dq, s);
+    if (int e = launch_status()) return e;
+  }
+  if (dk != nullptr || dv != nullptr) {
+    size_t sm = (2 * tile_floats(s.D) + 2 * simt::KT + simt::WARPS * 2 * s.D) * sizeof(float);
+    auto kern = simt::dkdv_col_kernel<T>;
+    set_smem(kern, sm);
+    kern<<<col_grid(s), simt::WARPS * 32, sm, st>>>((const T*)q, (const T*)k, (const T*)v,
+                                                    (const T*)dout, lse, z, (T*)dk, (T*)dv, s);
+    if (int e = launch_status()) return e;
+  }
+  return THERIA_OK;
+}
+
+template <typename T>
+int simt_jvp(const void* q, const void* k, const void* v, const void* tq, const void* tk,
+             const void* tv, const void* w, const float* lse, void* o_tan, float* stats,
+             const Shape& s, cudaStream_t st) {
+  size_t sm = (4 * tile_floats(s.D) + simt::WARPS * 3 * s.D) * sizeof(float);
+  auto kern = simt::jvp_row_kernel<T>;
+  set_smem(kern, sm);
+  kern<<<row_grid(s), simt::WARPS * 32, sm, st>>>(
+      (const T*)q, (const T*)k, (const T*)v, (const T*)tq, (const T*)tk, (const T*)tv,
+      (const T*)w, lse, (T*)o_tan, stats, s);
+  return launch_status();
+}
+
+template <typename T>
+int simt_hvp(const void* q, const void* k, const void* v, const void* w, const float* lse,
+             const void* tq, const void* tk, const void* tv, void* hq, void* hk, void* hv,
+             void* o_tan, float* stats, const Shape& s, cudaStream_t st) {
+  if (int e = simt_jvp<T>(q, k, v, tq, tk, tv, w, lse, o_tan, stats, s, st)) return e;
+  if (hq != nullptr) {
+    size_t sm = (4 * tile_floats(s.D) + simt::WARPS * 3 * s.D) * sizeof(float);
+    auto kern = simt::hq_row_kernel<T>;
+    set_smem(kern, sm);
+    kern<<<row_grid(s), simt::WARPS * 32, sm, st>>>(
+        (const T*)q, (const T*)k, (const T*)v, (const T*)tq, (const T*)tk, (const T*)tv,
+        (const T*)w, lse, stats, (T*)hq, s);
+    if (int e = launch_status()) return e;
+  }
+  if (hk != nullptr || hv != nullptr) {
+    size_t sm = (3 * tile_floats(s.D) + 4 * simt::KT + simt::WARPS * 4 * s.D) * sizeof(float);
+    auto kern = simt::hkhv_col_kernel<T>;
+    set_smem(kern, sm);
+    kern<<<col_grid(s), simt::WARPS * 32, sm, st>>>(
+        (const T*)q, (const T*)k, (const T*)v, (const T*)tq, (const T*)tk, (const T*)tv,
+        (const T*)w, lse, stats, (T*)hk, (T*)hv, s);
+    if (int e = launch_status()) return e;
+  }
+  return THERIA_OK;
+}
+
+#define THERIA_DISPATCH(dtype, FN, ...)                          \
+  ((dtype) == THERIA_F32   ? FN<float>(__VA_ARGS__)              \
+   : (dtype) == THERIA_F16 ? FN<__half>(__VA_ARGS__)             \
+                           : FN<__nv_bfloat16>(__VA_ARGS__))
+
+}  // namespace
+}  // namespace theria
+
+using namespace theria;
+
+extern "C" {
+
+const char* theria_status_string(int status) {
+  switch (status) {
+    case THERIA_OK: return "ok";
+    case THERIA_ERR_INVALID_ARG: return "invalid argument";
+    case THERIA_ERR_UNSUPPORTED: return "unsupported shape (head_dim <= 128, batch*heads <= 65535)";
+    case THERIA_ERR_LAUNCH: return "CUDA kernel launch failed";
+    case THERIA_ERR_WORKSPACE: return "workspace missing or too small";
+    case THERIA_ERR_DEVICE_TIMEOUT: return "device-side wait timed out";
+    default: return "unknown status";
+  }
+}
+
+const char* theria_version(void) { return "theria-sm100 0.1.0"; }
+
+int64_t theria_launch_count(void) { return (int64_t)launch_counter().load(); }
+
+int theria_sdpa_fwd(const void* q, const void* k, const void* v, void* o, int o_dtype,
+                    float* lse, int64_t B, int64_t H, int64_t T, int64_t M, int64_t D,
+                    int dtype, float scale, int causal, void* stream) {
+  if (int e = check_shape(B, H, T, M, D, dtype)) return e;
+  if (o_dtype != THERIA_F32 && o_dtype != dtype) return THERIA_ERR_INVALID_ARG;
+  if (empty_problem(B, H, T)) return THERIA_OK;
+  if (!q || !k || !v || !o) return THERIA_ERR_INVALID_ARG;
+  Shape s{B, H, T, M, D, scale, causal ? 1 : 0};
+  cudaStream_t st = (cudaStream_t)stream;
+  return THERIA_DISPATCH(dtype, simt_fwd, q, k, v, o, o_dtype, lse, s, st);
+}
+
+int64_t theria_sdpa_bwd_workspace_bytes(int64_t B, int64_t H, int64_t T, int64_t M,
+                                        int64_t D) {
+  (void)M;
+  (void)D;
+  return align_up(B * H * T * (int64_t)sizeof(float));
+}
+
+int64_t theria_sdpa_hvp_workspace_bytes(int64_t B, int64_t H, int64_t T, int64_t M,
+                                        int64_t D) {
+  (void)M;
+  (void)D;
+  return align_up(3 * B * H * T * (int64_t)sizeof(float));
+}
+
+int theria_sdpa_bwd(const void* q, const void* k, const void* v, const void* o, int o_dtype,
+                    const void* dout, const float* lse, void* dq, void* dk, void* dv,
+                    void* workspace, int64_t workspace_bytes, int64_t B, int64_t H, int64_t T,
+                    int64_t M, int64_t D, int dtype, float scale, int causal, void* stream) {
+  if (int e = check_shape(B, H, T, M, D, dtype)) return e;
+  if (o != nullptr && !valid_dtype(o_dtype)) return THERIA_ERR_INVALID_ARG;
+  if (empty_problem(B, H, T)) return THERIA_OK;
+  if (!q || !k || !v || !dout || !lse) return THERIA_ERR_INVALID_ARG;
+  if (!workspace || workspace_bytes < theria_sdpa_bwd_workspace_bytes(B, H, T, M, D))
+    return THERIA_ERR_WORKSPACE;
+  Shape s{B, H, T, M, D, scale, causal ? 1 : 0};
+  cudaStream_t st = (cudaStream_t)stream;
+  return THERIA_DISPATCH(dtype, simt_bwd, q, k, v, o, o_dtype, dout, lse, dq, dk, dv,
+                         (float*)workspace, s, st);
+}
+
+int theria_sdpa_jvp(const void* q, const void* k, const void* v, const void* tq,
+                    const void* tk, const void* tv, const float* lse, void* o_tan, int64_t B,
+                    int64_t H, int64_t T, int64_t M, int64_t D, int dtype, float scale,
+                    int causal, void* stream) {
+  if (int e = check_shape(B, H, T, M, D, dtype)) return e;
+  if (empty_problem(B, H, T)) return THERIA_OK;
+  if (!q || !k || !v || !tq || !tk || !tv || !lse || !o_tan) return THERIA_ERR_INVALID_ARG;
+  Shape s{B, H, T, M, D, scale, causal ? 1 : 0};
+  cudaStream_t st = (cudaStream_t)stream;
+  return THERIA_DISPATCH(dtype, simt_jvp, q, k, v, tq, tk, tv, nullptr, lse, o_tan, nullptr, s,
+                         st);
+}
+
+int theria_sdpa_hvp(const void* q, const void* k, const void* v, const void* w,
+                    const float* lse, const void* tq, const void* tk, const void* tv, void* hq,
+                    void* hk, void* hv, void* o_tan, void* workspace, int64_t workspace_bytes,
+                    int64_t B, int64_t H, int64_t T, int64_t M, int64_t D, int dtype,
+                    float scale, int causal, void* stream) {
+  if (int e = check_shape(B, H, T, M, D, dtype)) return e;
+  if (empty_problem(B, H, T)) return THERIA_OK;
+  if (!q || !k || !v || !w || !lse || !tq || !tk || !tv) return THERIA_ERR_INVALID_ARG;
+  if (!workspace || workspace_bytes < theria_sdpa_hvp_workspace_bytes(B, H, T, M, D))
+    return THERIA_ERR_WORKSPACE;
+  Shape s{B, H, T, M, D, scale, causal ? 1 : 0};
+  cudaStream_t st = (cudaStream_t)stream;
+  return THERIA_DISPATCH(dtype, simt_hvp, q, k, v, w, lse, tq, tk, tv, hq, hk, hv, o_tan,
+                         (float*)workspace, s, st);
+}
+
+int theria_get_device_error(int* out_flag, void* stream) {
+  if (!out_flag) return THERIA_ERR_INVALID_ARG;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (cudaMemcpyFromSymbolAsync(out_flag, g_device_error, sizeof(int), 0,
+                                cudaMemcpyDeviceToHost, st) != cudaSuccess)
+    return THERIA_ERR_LAUNCH;
+  return cudaStreamSynchronize(st) == cudaSuccess ? THERIA_OK : THERIA_ERR_LAUNCH;
+}
+
+int theria_clear_device_error(void* stream) {
+  static const int zero = 0;
+  return cudaMemcpyToSymbolAsync(g_device_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice,
+                                 (cudaStream_t)stream) == cudaSuccess
+             ? THERIA_OK
+             : THERIA_ERR_LAUNCH;
+}
+
+}  // extern "C"
