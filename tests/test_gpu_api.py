@@ -160,3 +160,24 @@ def test_fp32_double_backward_cfg1():
                     vv.double(), eps=1e-3)
     for a, b in zip(h, fd):
         assert max_rel(a, b) <= 1e-4
+
+
+def test_double_backward_through_strided_views():
+    # Heads split out of a fused projection arrive as non-contiguous views;
+    # the second-order path must still reach the tensor they view.
+    g = torch.Generator("cpu").manual_seed(7)
+    x = torch.randn(2, 48, 3, 2, 16, generator=g)  # (B, T, qkv, H, D)
+    w, tq = torch.randn(2, 2, 48, 16, generator=g), torch.randn(2, 48, 3, 2, 16, generator=g)
+    xd = x.to(DEV).requires_grad_(True)
+    q, k, v = xd.permute(2, 0, 3, 1, 4)
+    assert not q.is_contiguous()
+    out = sdpa(q, k, v)
+    (gx,) = torch.autograd.grad((out * w.to(DEV)).sum(), (xd,), create_graph=True)
+    (hx,) = torch.autograd.grad((gx * tq.to(DEV)).sum(), (xd,))
+    xc = x.double().requires_grad_(True)
+    qc, kc, vc = xc.permute(2, 0, 3, 1, 4)
+    (gc,) = torch.autograd.grad((orc.attention(qc, kc, vc) * w.double()).sum(), (xc,),
+                                create_graph=True)
+    (hc,) = torch.autograd.grad((gc * tq.double()).sum(), (xc,))
+    assert max_rel(gx, gc) <= 1e-5
+    assert max_rel(hx, hc) <= 1e-4

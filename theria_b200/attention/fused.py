@@ -35,9 +35,13 @@ class SDPABackward(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, q, k, v, o, lse, dout, causal, scale):
+        # q, k, v are the forward's own inputs (possibly strided views): they
+        # must stay the tensors autograd knows, or the second-order path
+        # through them is cut.  Packed copies feed the kernels only.
+        qc, kc, vc = q.contiguous(), k.contiguous(), v.contiguous()
         dout = _c(dout, q.dtype)
-        dq, dk, dv = ops.backward(q, k, v, dout, lse, o=o, causal=causal, scale=scale)
-        ctx.save_for_backward(q, k, v, lse, dout)
+        dq, dk, dv = ops.backward(qc, kc, vc, dout, lse, o=o, causal=causal, scale=scale)
+        ctx.save_for_backward(qc, kc, vc, lse, dout)
         ctx.causal, ctx.scale = causal, scale
         return dq, dk, dv
 
@@ -62,9 +66,10 @@ class SDPAFunction(torch.autograd.Function):
     def forward(ctx, q, k, v, causal=False, scale=None):
         scale = ops.default_scale(q) if scale is None else float(scale)
         # Strided views (e.g. heads split out of a fused projection) are
-        # packed once here; the kernels read contiguous [B, H, N, D].
-        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
-        o, lse = ops.forward(q, k, v, causal=causal, scale=scale)
+        # packed for the kernels, but the saved q, k, v are the inputs
+        # themselves so that the backward Function stays connected to them.
+        o, lse = ops.forward(q.contiguous(), k.contiguous(), v.contiguous(), causal=causal,
+                             scale=scale)
         ctx.save_for_backward(q, k, v, o, lse)
         ctx.causal, ctx.scale = causal, scale
         return o

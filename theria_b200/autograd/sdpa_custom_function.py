@@ -21,8 +21,10 @@ class SDPACustom(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, causal=False):
         scale = ops.default_scale(q)
-        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
-        o, lse = ops.forward(q, k, v, causal=causal, scale=scale)
+        # Save the inputs themselves (not packed copies): the backward
+        # Function must stay connected to them for second order.
+        o, lse = ops.forward(q.contiguous(), k.contiguous(), v.contiguous(), causal=causal,
+                             scale=scale)
         ctx.save_for_backward(q, k, v, o, lse)
         ctx.causal, ctx.scale = causal, scale
         return o
