@@ -35,6 +35,8 @@ extern "C" {
 #define THERIA_ERR_LAUNCH 3       /* a CUDA launch returned an error     */
 #define THERIA_ERR_WORKSPACE 4    /* workspace missing or too small      */
 #define THERIA_ERR_DEVICE_TIMEOUT 5 /* a device-side wait gave up        */
+#define THERIA_ERR_SCRATCH_LIMIT 6 /* problem exceeds the fixed scratch of
+                                      theria_sdpa_bwd_noalloc            */
 
 /* element types */
 #define THERIA_F32 0
@@ -115,6 +117,36 @@ int theria_sdpa_hvp(const void* q, const void* k, const void* v,
                     void* workspace, int64_t workspace_bytes,
                     int64_t B, int64_t H, int64_t T, int64_t M, int64_t D,
                     int dtype, float scale, int causal, void* stream);
+
+/*
+ * Allocation-free backward.  No counterpart in the reference library.
+ *
+ * Same arguments, outputs and results as theria_sdpa_bwd, minus the
+ * workspace: the scratch it needs (one float per query row) lives in a
+ * fixed array inside the library, THERIA_NOALLOC_SCRATCH_BYTES per GPU,
+ * held by every GPU that loads the library until the process exits.  It is
+ * for callers that cannot allocate device memory at call time -- code
+ * running under a foreign allocator or memory pool that forbids
+ * cudaMalloc, or a host that has no allocator handle at all (a plain C
+ * caller holding only raw pointers).  This entry point performs no device
+ * allocation of any kind.
+ *
+ * Limits: B*H*T*4 bytes must fit in THERIA_NOALLOC_SCRATCH_BYTES, else it
+ * returns THERIA_ERR_SCRATCH_LIMIT without launching anything.  All calls
+ * on a GPU share the one array, so calls that overlap on the GPU (two
+ * streams, or two host threads on different streams) race and corrupt each
+ * other's results; serialise them.  The first call on each device looks up
+ * the array's device address with that device current (one-time set-up);
+ * make that first call before any stream capture.  The array keeps the last
+ * call's contents; nothing in it needs to start at zero (every element a
+ * call reads was written earlier in that same call).
+ */
+#define THERIA_NOALLOC_SCRATCH_BYTES (4 * 1024 * 1024)
+int theria_sdpa_bwd_noalloc(const void* q, const void* k, const void* v,
+                            const void* o, int o_dtype, const void* dout,
+                            const float* lse, void* dq, void* dk, void* dv,
+                            int64_t B, int64_t H, int64_t T, int64_t M, int64_t D,
+                            int dtype, float scale, int causal, void* stream);
 
 /* Number of kernels this library has launched in this process (all devices,
  * all threads); for accounting in benchmarks and tests. */

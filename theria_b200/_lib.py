@@ -21,6 +21,8 @@ THERIA_ERR_UNSUPPORTED = 2
 THERIA_ERR_LAUNCH = 3
 THERIA_ERR_WORKSPACE = 4
 THERIA_ERR_DEVICE_TIMEOUT = 5
+THERIA_ERR_SCRATCH_LIMIT = 6
+NOALLOC_SCRATCH_BYTES = 4 * 1024 * 1024
 
 F32, F16, BF16 = 0, 1, 2
 DTYPE_CODE = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
@@ -42,6 +44,7 @@ SIGNATURES = {
                              _i64, _i64, _i64, _i64, _i64, _i, _f, _i, _vp]),
     "theria_sdpa_jvp": (_i, [_vp] * 8 + [_i64] * 5 + [_i, _f, _i, _vp]),
     "theria_sdpa_hvp": (_i, [_vp] * 12 + [_vp, _i64] + [_i64] * 5 + [_i, _f, _i, _vp]),
+    "theria_sdpa_bwd_noalloc": (_i, [_vp] * 10 + [_i64] * 5 + [_i, _f, _i, _vp]),
     "theria_launch_count": (_i64, []),
     "theria_get_device_error": (_i, [ctypes.POINTER(ctypes.c_int), _vp]),
     "theria_clear_device_error": (_i, [_vp]),

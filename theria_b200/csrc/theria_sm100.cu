@@ -4,6 +4,7 @@
 // this file includes the kernel headers and implements argument checking,
 // workspace carving and kernel selection for each entry point.
 #include <cstdio>
+#include <mutex>
 
 #include "common.cuh"
 #include "sdpa_simt.cuh"
@@ -151,6 +152,9 @@ const char* theria_status_string(int status) {
     case THERIA_ERR_LAUNCH: return "CUDA kernel launch failed";
     case THERIA_ERR_WORKSPACE: return "workspace missing or too small";
     case THERIA_ERR_DEVICE_TIMEOUT: return "device-side wait timed out";
+    case THERIA_ERR_SCRATCH_LIMIT:
+      return "problem too large for the fixed scratch of theria_sdpa_bwd_noalloc "
+             "(B*H*T*4 bytes must fit in THERIA_NOALLOC_SCRATCH_BYTES); use theria_sdpa_bwd";
     default: return "unknown status";
   }
 }
@@ -245,6 +249,47 @@ int theria_clear_device_error(void* stream) {
                                  (cudaStream_t)stream) == cudaSuccess
              ? THERIA_OK
              : THERIA_ERR_LAUNCH;
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free backward.  Its scratch is this file-scope device array, one
+// copy per GPU that loads the library.  On the host, `g_noalloc_scratch` only
+// names the symbol: its device address is looked up once per device with
+// cudaGetSymbolAddress (with that device current) and cached.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[THERIA_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of the scratch array on the current device, or nullptr.
+void* noalloc_scratch_ptr() {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess) return nullptr;
+    g_noalloc_ptr[dev] = p;
+  }
+  return g_noalloc_ptr[dev];
+}
+}  // namespace
+
+int theria_sdpa_bwd_noalloc(const void* q, const void* k, const void* v, const void* o,
+                            int o_dtype, const void* dout, const float* lse, void* dq,
+                            void* dk, void* dv, int64_t B, int64_t H, int64_t T, int64_t M,
+                            int64_t D, int dtype, float scale, int causal, void* stream) {
+  if (int e = check_shape(B, H, T, M, D, dtype)) return e;
+  if (theria_sdpa_bwd_workspace_bytes(B, H, T, M, D) > (int64_t)THERIA_NOALLOC_SCRATCH_BYTES)
+    return THERIA_ERR_SCRATCH_LIMIT;
+  if (empty_problem(B, H, T)) return THERIA_OK;
+  void* scratch = noalloc_scratch_ptr();
+  if (scratch == nullptr) return THERIA_ERR_LAUNCH;
+  return theria_sdpa_bwd(q, k, v, o, o_dtype, dout, lse, dq, dk, dv, scratch,
+                         (int64_t)THERIA_NOALLOC_SCRATCH_BYTES, B, H, T, M, D, dtype, scale,
+                         causal, stream);
 }
 
 }  // extern "C"
