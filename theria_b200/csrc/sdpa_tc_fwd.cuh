@@ -1,0 +1,309 @@
+// Tensor-core (tcgen05) SDPA forward for bf16/fp16 with head dim 64 or 128.
+//
+// One CTA owns a 128-row query tile of one (batch, head) and streams the
+// keys in tiles of 128.  Warp roles:
+//   warp 0      TMA producer: Q once, then K and V tiles into a 2-stage ring
+//   warp 1      MMA issuer (one thread) and TMEM owner
+//   warps 2..5  softmax + epilogue, one query row per thread (TMEM lane)
+// TMEM (512 columns): S double buffer at columns [0,128) and [128,256),
+// the O accumulator at [256, 256+HD).
+// Per key tile j the MMA thread issues S_{j+1} = Q K_{j+1}^T before waiting
+// for P_j, so the QK^T of the next tile overlaps this tile's softmax, then
+// O += P_j V_j with P_j (16-bit, written by the softmax warps into a
+// double-buffered SW128 shared tile) as the A operand and V as an MN-major
+// B operand.
+// Softmax runs in the log2 domain with a lazily updated row maximum: O and
+// l are rescaled only when the running maximum grows by more than 8 (P stays
+// <= 2^8, fp32 cannot overflow); the final O / l is exact either way.  The
+// epilogue writes O (input dtype or fp32) and LSE = ln(2) * (m + log2 l).
+#pragma once
+
+#include "tc_common.cuh"
+
+namespace theria {
+namespace tcfwd {
+
+constexpr int BM = 128;      // query rows per CTA
+constexpr int BN = 128;      // keys per tile
+constexpr int STAGES = 2;    // K/V ring depth
+constexpr int NTHREADS = 192;
+constexpr float kRescaleThreshold = 8.f;  // log2 units
+
+template <int HD>
+struct Smem {
+  static constexpr int kQ = BM * HD * 2;
+  static constexpr int kKV = BN * HD * 2;
+  static constexpr int kP = BM * BN * 2;
+  static constexpr int oQ = 0;
+  static constexpr int oK = oQ + kQ;
+  static constexpr int oV = oK + STAGES * kKV;
+  static constexpr int oP = oV + STAGES * kKV;
+  static constexpr int oBar = oP + 2 * kP;
+  // barriers: q_full, k_full[S], v_full[S], kv_empty[S], s_full[2],
+  // p_full[2], o_done[2], drain
+  static constexpr int nBar = 1 + 3 * STAGES + 6 + 1;
+  static constexpr int oTmem = oBar + nBar * 8;
+  static constexpr int oAbort = oTmem + 4;
+  static constexpr int kBytes = oAbort + 4;
+  static constexpr int kAlloc = kBytes + 1024;  // slack to align the base to 1024
+};
+
+template <typename T, int HD, bool CAUSAL>
+__global__ void __launch_bounds__(NTHREADS, 1)
+fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+           const __grid_constant__ CUtensorMap tm_v, void* __restrict__ out, int out_f32,
+           float* __restrict__ lse, int Tq, int M, float scale_log2) {
+  using L = Smem<HD>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::oBar);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* v_full = k_full + STAGES;
+  uint64_t* kv_empty = v_full + STAGES;
+  uint64_t* s_full = kv_empty + STAGES;
+  uint64_t* p_full = s_full + 2;
+  uint64_t* o_done = p_full + 2;
+  uint64_t* drain = o_done + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::oTmem);
+  volatile int* abort = reinterpret_cast<volatile int*>(smem + L::oAbort);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.y;
+  const int qt = CAUSAL ? (gridDim.x - 1 - blockIdx.x) : blockIdx.x;  // heavy tiles first
+  const int q0 = qt * BM;
+  int n_tiles = (M + BN - 1) / BN;
+  if (CAUSAL) n_tiles = min(n_tiles, (q0 + BM - 1) / BN + 1);
+
+  if (threadIdx.x == 0) {
+    tc::mbar_init(q_full, 1);
+    for (int s = 0; s < STAGES; ++s) {
+      tc::mbar_init(k_full + s, 1);
+      tc::mbar_init(v_full + s, 1);
+      tc::mbar_init(kv_empty + s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      tc::mbar_init(s_full + b, 1);
+      tc::mbar_init(p_full + b, 128);
+      tc::mbar_init(o_done + b, 1);
+    }
+    tc::mbar_init(drain, 1);
+    *abort = 0;
+    tc::fence_barrier_init();
+  }
+  if (warp == 1) tc::tmem_alloc(tmem_slot, 512);
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t t_o = tmem + 256;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tc::prefetch_tmap(&tm_q);
+      tc::prefetch_tmap(&tm_k);
+      tc::prefetch_tmap(&tm_v);
+      int issued = 0;
+      tc::mbar_expect_tx(q_full, L::kQ);
+      for (int cb = 0; cb < HD / 64; ++cb)
+        tc::tma_load_3d(smem + L::oQ + cb * BM * 128, &tm_q, q_full, cb * 64, q0, bh);
+      for (int j = 0; j < n_tiles; ++j) {
+        const int st = j % STAGES;
+        if (j >= STAGES && !tc::mbar_wait(kv_empty + st, ((j / STAGES) - 1) & 1, abort)) break;
+        tc::mbar_expect_tx(k_full + st, L::kKV);
+        for (int cb = 0; cb < HD / 64; ++cb)
+          tc::tma_load_3d(smem + L::oK + st * L::kKV + cb * BN * 128, &tm_k, k_full + st,
+                          cb * 64, j * BN, bh);
+        tc::mbar_expect_tx(v_full + st, L::kKV);
+        for (int cb = 0; cb < HD / 64; ++cb)
+          tc::tma_load_3d(smem + L::oV + st * L::kKV + cb * BN * 128, &tm_v, v_full + st,
+                          cb * 64, j * BN, bh);
+        issued = j + 1;
+      }
+      // Every copy issued into this CTA's shared memory lands before it may
+      // exit (bounded; returns at once on the normal path).
+      tc::mbar_wait_drain(q_full, 0);
+      for (int j = issued > STAGES ? issued - STAGES : 0; j < issued; ++j) {
+        tc::mbar_wait_drain(k_full + j % STAGES, (j / STAGES) & 1);
+        tc::mbar_wait_drain(v_full + j % STAGES, (j / STAGES) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t id_s = tc::idesc_f16(BM, BN, tc::AbFmt<T>::v, 0, 0);
+      constexpr uint32_t id_pv = tc::idesc_f16(BM, HD, tc::AbFmt<T>::v, 0, 1);
+      const uint32_t q_addr = tc::smem_u32(smem + L::oQ);
+      auto issue_s = [&](int j) -> bool {
+        const int st = j % STAGES;
+        if (!tc::mbar_wait(k_full + st, (j / STAGES) & 1, abort)) return false;
+        tc::tc_fence_after();
+        const uint32_t k_addr = tc::smem_u32(smem + L::oK + st * L::kKV);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off_q = (kk / 4) * (BM * 128) + (kk % 4) * 32;
+          const uint32_t off_k = (kk / 4) * (BN * 128) + (kk % 4) * 32;
+          tc::mma_ss(tmem + (j & 1) * 128, tc::sw128_desc(q_addr + off_q, 16, 1024),
+                     tc::sw128_desc(k_addr + off_k, 16, 1024), id_s, kk > 0 ? 1u : 0u);
+        }
+        tc::mma_commit(s_full + (j & 1));
+        return true;
+      };
+      bool ok = tc::mbar_wait(q_full, 0, abort);
+      if (ok) tc::tc_fence_after();
+      if (ok) ok = issue_s(0);
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        const int st = j % STAGES;
+        if (j + 1 < n_tiles && !issue_s(j + 1)) break;
+        if (!tc::mbar_wait(p_full + (j & 1), (j >> 1) & 1, abort)) break;
+        if (!tc::mbar_wait(v_full + st, (j / STAGES) & 1, abort)) break;
+        tc::tc_fence_after();
+        const uint32_t p_addr = tc::smem_u32(smem + L::oP + (j & 1) * L::kP);
+        const uint32_t v_addr = tc::smem_u32(smem + L::oV + st * L::kKV);
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const uint32_t off_p = (kk / 4) * (BM * 128) + (kk % 4) * 32;
+          tc::mma_ss(t_o, tc::sw128_desc(p_addr + off_p, 16, 1024),
+                     tc::sw128_desc(v_addr + kk * 16 * 128, BN * 128, 1024), id_pv,
+                     (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc::mma_commit(o_done + (j & 1));
+        tc::mma_commit(kv_empty + st);
+      }
+      // Every MMA issued above completes before TMEM is freed.
+      tc::mma_commit(drain);
+      tc::mbar_wait_drain(drain, 0);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int quarter = warp & 3;        // TMEM lanes this warp may access
+    const int r = quarter * 32 + lane;   // row within the tile
+    const int row = q0 + r;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    // Waits are warp-uniform: the TMEM loads that follow are warp-collective.
+    auto wait = [&](uint64_t* bar, uint32_t parity) {
+      return __all_sync(0xffffffffu, tc::mbar_wait(bar, parity, abort));
+    };
+    for (int j = 0; j < n_tiles; ++j) {
+      if (!wait(s_full + (j & 1), (j >> 1) & 1)) { ok = false; break; }
+      tc::tc_fence_after();
+      float x[BN];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        float v[32];
+        tc::tmem_ld32(tmem + (j & 1) * 128 + lane_off + c * 32, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) x[c * 32 + i] = v[i] * scale_log2;
+      }
+      const int col0 = j * BN;
+      if ((col0 + BN > M) || (CAUSAL && col0 + BN - 1 > q0)) {
+#pragma unroll
+        for (int i = 0; i < BN; ++i) {
+          const int col = col0 + i;
+          if (col >= M || (CAUSAL && col > row)) x[i] = -INFINITY;
+        }
+      }
+      float mt = x[0];
+#pragma unroll
+      for (int i = 1; i < BN; ++i) mt = fmaxf(mt, x[i]);
+      const float m_new = fmaxf(m, mt);
+      float m_use = m;
+      bool rescale = false;
+      if (m == -INFINITY) {
+        m_use = m_new;
+      } else if (m_new - m > kRescaleThreshold) {
+        m_use = m_new;
+        rescale = true;
+      }
+      const float m_sub = (m_use == -INFINITY) ? 0.f : m_use;
+      float rowsum = 0.f;
+#pragma unroll
+      for (int i = 0; i < BN; ++i) {
+        x[i] = tc::ex2(x[i] - m_sub);
+        rowsum += x[i];
+      }
+      if (__any_sync(0xffffffffu, rescale)) {
+        // O holds PV_0..PV_{j-1}: wait for the last of them before touching it.
+        if (!wait(o_done + ((j - 1) & 1), ((j - 1) >> 1) & 1)) { ok = false; break; }
+        tc::tc_fence_after();
+        const float alpha = rescale ? tc::ex2(m - m_use) : 1.f;
+        l *= alpha;
+#pragma unroll
+        for (int c = 0; c < HD / 32; ++c) {
+          float v[32];
+          tc::tmem_ld32(t_o + lane_off + c * 32, v);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] *= alpha;
+          tc::tmem_st32(t_o + lane_off + c * 32, v);
+        }
+        tc::tmem_wait_st();
+      }
+      l += rowsum;
+      m = m_use;
+      // P buffer (j & 1) was last read by PV_{j-2}.
+      if (j >= 2 && !wait(o_done + (j & 1), ((j - 2) >> 1) & 1)) { ok = false; break; }
+      const uint32_t p_addr = tc::smem_u32(smem + L::oP + (j & 1) * L::kP);
+#pragma unroll
+      for (int cb = 0; cb < BN / 64; ++cb) {
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch) {
+          const float* e = x + cb * 64 + ch * 8;
+          tc::st_shared_v4(p_addr + cb * (BM * 128) + tc::sw128_off(r, ch),
+                           tc::pack2<T>(e[0], e[1]), tc::pack2<T>(e[2], e[3]),
+                           tc::pack2<T>(e[4], e[5]), tc::pack2<T>(e[6], e[7]));
+        }
+      }
+      tc::fence_proxy_async_smem();
+      tc::tc_fence_before();
+      tc::mbar_arrive(p_full + (j & 1));
+    }
+    // ------------------------------------------------------------ epilogue
+    const int jl = n_tiles - 1;
+    if (ok && wait(o_done + (jl & 1), (jl >> 1) & 1)) {
+      tc::tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const bool store = row < Tq;
+      const size_t base = ((size_t)bh * Tq + (size_t)(store ? row : 0)) * HD;
+#pragma unroll
+      for (int c = 0; c < HD / 32; ++c) {
+        float v[32];
+        tc::tmem_ld32(t_o + lane_off + c * 32, v);  // warp-collective: before any branch
+        if (!store) continue;
+        if (out_f32) {
+          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(out) + base + c * 32);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            dst[i] = make_float4(v[4 * i] * inv, v[4 * i + 1] * inv, v[4 * i + 2] * inv,
+                                 v[4 * i + 3] * inv);
+        } else {
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<T*>(out) + base + c * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float* e = v + 8 * i;
+            dst[i] = make_uint4(tc::pack2<T>(e[0] * inv, e[1] * inv),
+                                tc::pack2<T>(e[2] * inv, e[3] * inv),
+                                tc::pack2<T>(e[4] * inv, e[5] * inv),
+                                tc::pack2<T>(e[6] * inv, e[7] * inv));
+          }
+        }
+      }
+      if (store && lse != nullptr)
+        lse[(size_t)bh * Tq + row] =
+            l > 0.f ? (m + log2f(l)) * 0.69314718055994531f : -INFINITY;
+    }
+  }
+  // ------------------------------------------------------------ teardown
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace tcfwd
+}  // namespace theria

@@ -1,0 +1,253 @@
+// sm_100a building blocks for the tensor-core kernels: mbarriers with
+// bounded waits, TMA tensor loads, tcgen05 (TMEM allocation, MMA issue,
+// commit, TMEM loads/stores) and the shared-memory matrix descriptors.
+//
+// Conventions used by every kernel here:
+//  * Operand tiles are bf16/fp16 with 128-byte rows ("SW128" atoms): a tile
+//    of R rows x 64 elements is R*128 bytes, rows grouped 8 to a 1024-byte
+//    atom, 16-byte chunk c of row r stored at chunk (c ^ (r & 7)).  TMA writes
+//    this layout with CU_TENSOR_MAP_SWIZZLE_128B; kernels that write a tile
+//    from registers use the same formula.  Tiles start on 1024-byte bounds.
+//  * A tile with more than 64 elements per row is a sequence of such
+//    64-wide column blocks, each R*128 bytes.
+//  * Every wait is bounded: on running out it sets the device error word and
+//    reports failure, and the kernel unwinds (no trap, no endless spin).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+
+namespace theria {
+namespace tc {
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---------------------------------------------------------------- mbarrier
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Upper bound on polls of one barrier phase.  try_wait itself suspends for
+// a hardware-chosen interval per poll, so this is far beyond any legitimate
+// wait in these kernels (a tile takes microseconds).
+constexpr uint32_t kMaxPolls = 1u << 22;
+
+// Wait for the phase with the given parity to complete.  Returns false (and
+// sets the device error word) if it does not within kMaxPolls polls, or if
+// another thread of the CTA already gave up (*abort != 0).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          volatile int* abort) {
+  for (uint32_t i = 0; i < kMaxPolls; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 1023) == 1023 && *abort) return false;
+  }
+  *abort = 1;
+  atomicExch(&g_device_error, THERIA_ERR_DEVICE_TIMEOUT);
+  return false;
+}
+
+// Bounded wait that ignores the abort flag: used at teardown to let copies
+// or MMAs already in flight land before the CTA exits.
+__device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kMaxPolls; ++i)
+    if (mbar_try_wait(bar, parity)) return;
+  atomicExch(&g_device_error, THERIA_ERR_DEVICE_TIMEOUT);
+}
+
+// ---------------------------------------------------------------- fences
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Named barrier among `count` threads (a multiple of 32).
+__device__ __forceinline__ void named_bar(uint32_t id, uint32_t count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// ---------------------------------------------------------------- TMA
+// 3-D tiled load of box {64 elems, rows, 1} at (x, y, z) into smem,
+// completing on `bar` (transaction bytes).  x must be 16-byte aligned in
+// elements (a multiple of 8 for 16-bit types): every caller passes 0 or 64.
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// ---------------------------------------------------------------- tcgen05
+// Allocate `ncols` TMEM columns (power of two >= 32); one full warp calls
+// it and the base address lands in *dst (shared memory).
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr),
+               "r"(ncols)
+               : "memory");
+}
+
+// D[tmem] (+)= A[smem] * B[smem], one instruction (M x N x 16).
+__device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                       uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive once on `bar` when every MMA this thread issued so far completes.
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+#define THERIA_R32(i) "=r"(r[i])
+// Warp-collective load of 32 consecutive fp32 columns of this warp's 32
+// TMEM lanes: thread t gets lane (base lane + t), columns col..col+31.  The
+// wait is in the same asm statement so no use of the registers can be
+// scheduled before the data has landed.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : THERIA_R32(0), THERIA_R32(1), THERIA_R32(2), THERIA_R32(3), THERIA_R32(4),
+        THERIA_R32(5), THERIA_R32(6), THERIA_R32(7), THERIA_R32(8), THERIA_R32(9),
+        THERIA_R32(10), THERIA_R32(11), THERIA_R32(12), THERIA_R32(13), THERIA_R32(14),
+        THERIA_R32(15), THERIA_R32(16), THERIA_R32(17), THERIA_R32(18), THERIA_R32(19),
+        THERIA_R32(20), THERIA_R32(21), THERIA_R32(22), THERIA_R32(23), THERIA_R32(24),
+        THERIA_R32(25), THERIA_R32(26), THERIA_R32(27), THERIA_R32(28), THERIA_R32(29),
+        THERIA_R32(30), THERIA_R32(31)
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+#undef THERIA_R32
+
+#define THERIA_F32R(i) "r"(__float_as_uint(v[i]))
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
+      "%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(
+          taddr),
+      THERIA_F32R(0), THERIA_F32R(1), THERIA_F32R(2), THERIA_F32R(3), THERIA_F32R(4),
+      THERIA_F32R(5), THERIA_F32R(6), THERIA_F32R(7), THERIA_F32R(8), THERIA_F32R(9),
+      THERIA_F32R(10), THERIA_F32R(11), THERIA_F32R(12), THERIA_F32R(13), THERIA_F32R(14),
+      THERIA_F32R(15), THERIA_F32R(16), THERIA_F32R(17), THERIA_F32R(18), THERIA_F32R(19),
+      THERIA_F32R(20), THERIA_F32R(21), THERIA_F32R(22), THERIA_F32R(23), THERIA_F32R(24),
+      THERIA_F32R(25), THERIA_F32R(26), THERIA_F32R(27), THERIA_F32R(28), THERIA_F32R(29),
+      THERIA_F32R(30), THERIA_F32R(31)
+      : "memory");
+}
+#undef THERIA_F32R
+
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// ---------------------------------------------------------------- descriptors
+// Shared-memory matrix descriptor for a 128-byte-swizzled tile.
+//   K-major  (contraction dim contiguous): lbo unused (16), sbo = 1024.
+//   MN-major (M/N dim contiguous): lbo = bytes between 64-element M/N
+//            blocks, sbo = bytes between groups of 8 contraction rows (1024).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// Instruction descriptor of kind::f16 with an fp32 accumulator.
+// ab_bf16: 1 = bf16 operands, 0 = fp16.  a_mn/b_mn: 1 = MN-major operand.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, int ab_bf16, int a_mn, int b_mn) {
+  return (1u << 4) | ((uint32_t)ab_bf16 << 7) | ((uint32_t)ab_bf16 << 10) |
+         ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) | ((uint32_t)(N >> 3) << 17) |
+         ((uint32_t)(M >> 4) << 24);
+}
+
+// Byte offset of 16-byte chunk `c` (0..7) of row `r` inside a SW128 block.
+__device__ __forceinline__ uint32_t sw128_off(uint32_t r, uint32_t c) {
+  return r * 128u + ((c ^ (r & 7u)) << 4);
+}
+
+template <typename T> __device__ __forceinline__ uint32_t pack2(float a, float b);
+template <> __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+template <> __device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <typename T> struct AbFmt;
+template <> struct AbFmt<__nv_bfloat16> { static constexpr int v = 1; };
+template <> struct AbFmt<__half> { static constexpr int v = 0; };
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
+               "r"(d)
+               : "memory");
+}
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+}  // namespace tc
+}  // namespace theria

@@ -4,10 +4,13 @@
 // this file includes the kernel headers and implements argument checking,
 // workspace carving and kernel selection for each entry point.
 #include <cstdio>
+#include <initializer_list>
 #include <mutex>
 
 #include "common.cuh"
 #include "sdpa_simt.cuh"
+#include "sdpa_tc_fwd.cuh"
+#include "tc_host.cuh"
 
 namespace theria {
 namespace {
@@ -132,6 +135,45 @@ int simt_hvp(const void* q, const void* k, const void* v, const void* w, const f
   return THERIA_OK;
 }
 
+// ------------------------------------------------------ tensor-core launches
+template <typename T, int HD, bool CAUSAL>
+int tc_fwd_launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, void* o,
+                  int out_f32, float* lse, const Shape& s, cudaStream_t st) {
+  auto kern = tcfwd::fwd_kernel<T, HD, CAUSAL>;
+  constexpr int smem = tcfwd::Smem<HD>::kAlloc;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  dim3 grid((unsigned)((s.T + tcfwd::BM - 1) / tcfwd::BM), (unsigned)(s.B * s.H));
+  kern<<<grid, tcfwd::NTHREADS, smem, st>>>(mq, mk, mv, o, out_f32, lse, (int)s.T, (int)s.M,
+                                            s.scale * 1.4426950408889634f);
+  return launch_status();
+}
+
+// Returns -1 when no TMA descriptor can describe the tensors (the caller
+// then runs the SIMT kernel), else a THERIA_* status.
+template <typename T>
+int tc_fwd(const void* q, const void* k, const void* v, void* o, int o_dtype, float* lse,
+           const Shape& s, int dtype, cudaStream_t st) {
+  CUtensorMap mq, mk, mv;
+  const int64_t bh = s.B * s.H;
+  if (!tc::make_map_3d(&mq, q, dtype, bh, s.T, s.D, tcfwd::BM) ||
+      !tc::make_map_3d(&mk, k, dtype, bh, s.M, s.D, tcfwd::BN) ||
+      !tc::make_map_3d(&mv, v, dtype, bh, s.M, s.D, tcfwd::BN))
+    return -1;
+  const int f32 = o_dtype == THERIA_F32;
+  if (s.D == 64)
+    return s.causal ? tc_fwd_launch<T, 64, true>(mq, mk, mv, o, f32, lse, s, st)
+                    : tc_fwd_launch<T, 64, false>(mq, mk, mv, o, f32, lse, s, st);
+  return s.causal ? tc_fwd_launch<T, 128, true>(mq, mk, mv, o, f32, lse, s, st)
+                  : tc_fwd_launch<T, 128, false>(mq, mk, mv, o, f32, lse, s, st);
+}
+
+bool use_tc(int dtype, const Shape& s, std::initializer_list<const void*> ptrs) {
+  if (!tc::tc_eligible(dtype, s.T, s.M, s.D, s.B * s.H)) return false;
+  for (const void* p : ptrs)
+    if (p != nullptr && !tc::aligned16(p)) return false;
+  return true;
+}
+
 #define THERIA_DISPATCH(dtype, FN, ...)                          \
   ((dtype) == THERIA_F32   ? FN<float>(__VA_ARGS__)              \
    : (dtype) == THERIA_F16 ? FN<__half>(__VA_ARGS__)             \
@@ -172,6 +214,11 @@ int theria_sdpa_fwd(const void* q, const void* k, const void* v, void* o, int o_
   if (!q || !k || !v || !o) return THERIA_ERR_INVALID_ARG;
   Shape s{B, H, T, M, D, scale, causal ? 1 : 0};
   cudaStream_t st = (cudaStream_t)stream;
+  if (use_tc(dtype, s, {q, k, v, o})) {
+    int e = dtype == THERIA_BF16 ? tc_fwd<__nv_bfloat16>(q, k, v, o, o_dtype, lse, s, dtype, st)
+                                 : tc_fwd<__half>(q, k, v, o, o_dtype, lse, s, dtype, st);
+    if (e >= 0) return e;
+  }
   return THERIA_DISPATCH(dtype, simt_fwd, q, k, v, o, o_dtype, lse, s, st);
 }
 
