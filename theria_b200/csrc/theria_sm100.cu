@@ -3,12 +3,14 @@
 // The whole library is one translation unit (no relocatable device code):
 // this file includes the kernel headers and implements argument checking,
 // workspace carving and kernel selection for each entry point.
+#include <algorithm>
 #include <cstdio>
 #include <initializer_list>
 #include <mutex>
 
 #include "common.cuh"
 #include "sdpa_simt.cuh"
+#include "sdpa_tc_bwd.cuh"
 #include "sdpa_tc_fwd.cuh"
 #include "tc_host.cuh"
 
@@ -167,6 +169,70 @@ int tc_fwd(const void* q, const void* k, const void* v, void* o, int o_dtype, fl
                   : tc_fwd_launch<T, 128, false>(mq, mk, mv, o, f32, lse, s, st);
 }
 
+int64_t simt_bwd_ws(const Shape& s) { return align_up(s.B * s.H * s.T * 4); }
+int64_t tc_bwd_ws(const Shape& s) {
+  return align_up(s.B * s.H * s.T * 4) + align_up(s.B * s.H * s.T * s.D * 4);
+}
+
+template <typename T, int HD, bool CAUSAL>
+int tc_bwd_launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                  const CUtensorMap& mdo, const float* lse, const float* z, float* dq_acc,
+                  void* dk, void* dv, const Shape& s, cudaStream_t st) {
+  auto kern = tcbwd::bwd_kernel<T, HD, CAUSAL>;
+  constexpr int smem = tcbwd::Smem<HD>::kAlloc;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  dim3 grid((unsigned)((s.M + tcbwd::BK - 1) / tcbwd::BK), (unsigned)(s.B * s.H));
+  kern<<<grid, tcbwd::NTHREADS, smem, st>>>(mq, mk, mv, mdo, lse, z, dq_acc, (T*)dk, (T*)dv,
+                                            (int)s.T, (int)s.M, s.scale,
+                                            s.scale * 1.4426950408889634f);
+  return launch_status();
+}
+
+// Tensor-core backward; -1 when no TMA descriptor fits (caller falls back).
+template <typename T>
+int tc_bwd(const void* q, const void* k, const void* v, const void* o, int o_dtype,
+           const void* dout, const float* lse, void* dq, void* dk, void* dv, void* ws,
+           const Shape& s, int dtype, cudaStream_t st) {
+  CUtensorMap mq, mk, mv, mdo;
+  const int64_t bh = s.B * s.H;
+  if (!tc::make_map_3d(&mq, q, dtype, bh, s.T, s.D, tcbwd::BQ) ||
+      !tc::make_map_3d(&mk, k, dtype, bh, s.M, s.D, tcbwd::BK) ||
+      !tc::make_map_3d(&mv, v, dtype, bh, s.M, s.D, tcbwd::BK) ||
+      !tc::make_map_3d(&mdo, dout, dtype, bh, s.T, s.D, tcbwd::BQ))
+    return -1;
+  float* z = (float*)ws;
+  float* dq_acc = (float*)((char*)ws + align_up(bh * s.T * 4));
+  const int64_t rows = bh * s.T;
+  if (o != nullptr) {
+    tcbwd::prep_kernel<T><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(
+        o, o_dtype == THERIA_F32, (const T*)dout, z, dq_acc, rows, (int)s.D);
+    if (int e = launch_status()) return e;
+  } else {
+    size_t sm = (2 * tile_floats(s.D) + simt::WARPS * 2 * s.D) * sizeof(float);
+    auto kern = simt::delta_from_stats_kernel<T>;
+    set_smem(kern, sm);
+    kern<<<row_grid(s), simt::WARPS * 32, sm, st>>>((const T*)q, (const T*)k, (const T*)v,
+                                                    (const T*)dout, lse, z, s);
+    if (int e = launch_status()) return e;
+    if (cudaMemsetAsync(dq_acc, 0, rows * s.D * 4, st) != cudaSuccess) return THERIA_ERR_LAUNCH;
+  }
+  int e;
+  if (s.D == 64)
+    e = s.causal ? tc_bwd_launch<T, 64, true>(mq, mk, mv, mdo, lse, z, dq_acc, dk, dv, s, st)
+                 : tc_bwd_launch<T, 64, false>(mq, mk, mv, mdo, lse, z, dq_acc, dk, dv, s, st);
+  else
+    e = s.causal ? tc_bwd_launch<T, 128, true>(mq, mk, mv, mdo, lse, z, dq_acc, dk, dv, s, st)
+                 : tc_bwd_launch<T, 128, false>(mq, mk, mv, mdo, lse, z, dq_acc, dk, dv, s, st);
+  if (e) return e;
+  if (dq != nullptr) {
+    const int64_t n = rows * s.D;
+    const unsigned blocks = (unsigned)std::min<int64_t>((n / 4 + 255) / 256, 148 * 16);
+    tcbwd::finish_kernel<T><<<blocks, 256, 0, st>>>(dq_acc, (T*)dq, n);
+    return launch_status();
+  }
+  return THERIA_OK;
+}
+
 bool use_tc(int dtype, const Shape& s, std::initializer_list<const void*> ptrs) {
   if (!tc::tc_eligible(dtype, s.T, s.M, s.D, s.B * s.H)) return false;
   for (const void* p : ptrs)
@@ -224,9 +290,10 @@ int theria_sdpa_fwd(const void* q, const void* k, const void* v, void* o, int o_
 
 int64_t theria_sdpa_bwd_workspace_bytes(int64_t B, int64_t H, int64_t T, int64_t M,
                                         int64_t D) {
-  (void)M;
-  (void)D;
-  return align_up(B * H * T * (int64_t)sizeof(float));
+  Shape s{B, H, T, M, D, 1.f, 0};
+  // Enough for the tensor-core path (row terms + fp32 dQ accumulator) where
+  // the head dim allows it; the CUDA-core path needs only the row terms.
+  return (D == 64 || D == 128) ? tc_bwd_ws(s) : simt_bwd_ws(s);
 }
 
 int64_t theria_sdpa_hvp_workspace_bytes(int64_t B, int64_t H, int64_t T, int64_t M,
@@ -244,10 +311,19 @@ int theria_sdpa_bwd(const void* q, const void* k, const void* v, const void* o, 
   if (o != nullptr && !valid_dtype(o_dtype)) return THERIA_ERR_INVALID_ARG;
   if (empty_problem(B, H, T)) return THERIA_OK;
   if (!q || !k || !v || !dout || !lse) return THERIA_ERR_INVALID_ARG;
-  if (!workspace || workspace_bytes < theria_sdpa_bwd_workspace_bytes(B, H, T, M, D))
-    return THERIA_ERR_WORKSPACE;
   Shape s{B, H, T, M, D, scale, causal ? 1 : 0};
+  if (!workspace || workspace_bytes < simt_bwd_ws(s)) return THERIA_ERR_WORKSPACE;
   cudaStream_t st = (cudaStream_t)stream;
+  // The tensor-core path needs the larger workspace; a caller that passes
+  // only the minimum (row terms) gets the CUDA-core kernels.
+  if (workspace_bytes >= tc_bwd_ws(s) && use_tc(dtype, s, {q, k, v, o, dout, dq, dk, dv})) {
+    int e = dtype == THERIA_BF16
+                ? tc_bwd<__nv_bfloat16>(q, k, v, o, o_dtype, dout, lse, dq, dk, dv, workspace, s,
+                                        dtype, st)
+                : tc_bwd<__half>(q, k, v, o, o_dtype, dout, lse, dq, dk, dv, workspace, s, dtype,
+                                 st);
+    if (e >= 0) return e;
+  }
   return THERIA_DISPATCH(dtype, simt_bwd, q, k, v, o, o_dtype, dout, lse, dq, dk, dv,
                          (float*)workspace, s, st);
 }
@@ -329,8 +405,7 @@ int theria_sdpa_bwd_noalloc(const void* q, const void* k, const void* v, const v
                             void* dk, void* dv, int64_t B, int64_t H, int64_t T, int64_t M,
                             int64_t D, int dtype, float scale, int causal, void* stream) {
   if (int e = check_shape(B, H, T, M, D, dtype)) return e;
-  if (theria_sdpa_bwd_workspace_bytes(B, H, T, M, D) > (int64_t)THERIA_NOALLOC_SCRATCH_BYTES)
-    return THERIA_ERR_SCRATCH_LIMIT;
+  if (B * H * T * 4 > (int64_t)THERIA_NOALLOC_SCRATCH_BYTES) return THERIA_ERR_SCRATCH_LIMIT;
   if (empty_problem(B, H, T)) return THERIA_OK;
   void* scratch = noalloc_scratch_ptr();
   if (scratch == nullptr) return THERIA_ERR_LAUNCH;
