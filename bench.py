@@ -197,7 +197,7 @@ def cpu_threads():
     return torch.get_num_threads()
 
 
-def cpu_fwdbwd_sample(budget_s=12.0, min_units=1, max_units=64, dtype=torch.bfloat16):
+def cpu_fwdbwd_sample(budget_s=12.0, min_units=1, max_units=4096, dtype=torch.bfloat16):
     """The CPU oracle's fwd+bwd (autograd through the restated forward, as the
     reference's CPU path computes it) on whole (b, h) units of configs[1],
     repeated until `budget_s` of CPU work.  Returns (TFLOP/s, units, seconds)."""
