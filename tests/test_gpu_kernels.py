@@ -73,6 +73,8 @@ SHAPES = [
     (1, 2, 130, 130, 64),
     (1, 1, 257, 257, 128),
     (1, 1, 200, 200, 48),  # head dim off the tensor-core list
+    (1, 2, 384, 640, 64),  # several key/query tiles, T < M
+    (1, 2, 640, 384, 128), # T > M: keys past every causal query row
 ]
 DTYPES = [torch.float32, torch.bfloat16, torch.float16]
 

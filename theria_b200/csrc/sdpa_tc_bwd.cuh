@@ -2,22 +2,24 @@
 //
 // Three launches per call:
 //   prep     z_i = rowsum(dO_i * O_i) and dQacc := 0        (memory bound)
-//   main     one CTA per (128-key tile, batch*head), looping over 128-row
-//            query tiles (key/value-stationary):
-//              S^T  = K Q_i^T            (tcgen05, TMEM cols [0,128))
-//              dP^T = V dO_i^T           (tcgen05, TMEM cols [128,256))
+//   main     one CTA per (128-key tile, batch*head), looping over 64-row
+//            query tiles t (key/value-stationary), double-buffered so the
+//            tensor core works on tile t+1 while CUDA cores finish tile t:
+//              S^T  = K Q_t^T,  dP^T = V dO_t^T      (tcgen05 -> TMEM)
 //              P^T  = exp(s S^T - LSE),  dS^T = P^T (dP^T - z)   (CUDA cores,
-//                     one key row per thread, written as 16-bit SW128 tiles)
-//              dV  += P^T dO_i           (TMEM cols [256, 256+D))
-//              dK  += dS^T Q_i           (TMEM cols [256+D, 256+2D))
-//              dQ_i = dS K               (TMEM cols [0, D), reusing S^T's)
-//            dQ_i is added to the fp32 accumulator dQacc with vector
-//            reductions (red.global.add.v4.f32); dK, dV are stored once.
-//   finish   dQ = scale * dQacc in the input dtype
-// Warp roles in main: warp 0 TMA, warp 1 MMA issuer + TMEM owner, warps
-// 2..5 compute.  Operand majors: K, Q_i as K-major (S^T), V, dO_i likewise
-// (dP^T); P^T / dS^T K-major with dO_i / Q_i MN-major (dV, dK); for dQ the
-// stored dS^T is read as an MN-major A and K as an MN-major B.
+//                     one key row per thread, 16-bit SW128 tiles in smem)
+//              dV  += P^T dO_t,  dK += dS^T Q_t       (TMEM accumulators)
+//              dQ   = dS K, added to the fp32 accumulator dQacc with
+//                     global reductions; dK, dV are stored once at the end.
+//   finish   dQ = dQacc in the input dtype (dQacc is pre-scaled)
+// TMEM (512 columns): buffer b in {0,1} holds S^T at [128b, 128b+64) and
+// dP^T at [128b+64, 128b+128); dV at [256, 256+D); dK at [256+D, 256+2D).
+// dQ: for D = 128 as dQ^T = K^T dS^T (M = D = 128 lanes, 64 columns) written
+// over the S^T of its own buffer once the CUDA cores have read it; for D = 64
+// as dQ = dS K for a PAIR of query tiles at once (M = 128 query rows, the
+// two adjacent dS^T buffers read as one MN-major operand) into [384, 448).
+// Warp roles: warp 0 TMA, warp 1 MMA issuer + TMEM owner, warps 2..9 two
+// groups of four (one per TMEM lane quarter) splitting the columns.
 #pragma once
 
 #include "tc_common.cuh"
@@ -25,23 +27,26 @@
 namespace theria {
 namespace tcbwd {
 
-constexpr int BK = 128;  // keys per CTA
-constexpr int BQ = 128;  // query rows per iteration
-constexpr int NTHREADS = 192;
+constexpr int BK = 128;        // keys per CTA (M of S^T, dP^T, dV, dK)
+constexpr int BQ = 64;         // query rows per iteration (N of S^T, dP^T)
+constexpr int NCOMPUTE = 256;  // 8 compute warps: 2 groups x 4 TMEM lane quarters
+constexpr int NTHREADS = 64 + NCOMPUTE;
 
 template <int HD>
 struct Smem {
-  static constexpr int kTile = 128 * HD * 2;  // one 128-row operand tile
-  static constexpr int kP = BK * BQ * 2;
+  static constexpr int kKV = BK * HD * 2;   // K or V tile
+  static constexpr int kQ = BQ * HD * 2;    // one Q or dO stage
+  static constexpr int kP = BK * BQ * 2;    // one P^T or dS^T buffer [key][q]
   static constexpr int oK = 0;
-  static constexpr int oV = oK + kTile;
-  static constexpr int oQ = oV + kTile;
-  static constexpr int oDO = oQ + kTile;
-  static constexpr int oP = oDO + kTile;     // P^T  [key][q]
-  static constexpr int oDS = oP + kP;        // dS^T [key][q]
-  static constexpr int oBar = oDS + kP;
-  // kv_full, qdo_full, qdo_empty, s_full, p_full, mma2_done, s_free, drain
-  static constexpr int nBar = 8;
+  static constexpr int oV = oK + kKV;
+  static constexpr int oQ = oV + kKV;       // 2 stages
+  static constexpr int oDO = oQ + 2 * kQ;   // 2 stages
+  static constexpr int oP = oDO + 2 * kQ;   // 2 buffers
+  static constexpr int oDS = oP + 2 * kP;   // 2 buffers (adjacent: a pair is one M=128 operand)
+  static constexpr int oBar = oDS + 2 * kP;
+  // kv_full, q_full[2], q_empty[2], s_full[2], p_full[2], mma2_done[2],
+  // s_free[2], dq_free, drain
+  static constexpr int nBar = 1 + 2 * 6 + 2;
   static constexpr int oTmem = oBar + nBar * 8;
   static constexpr int oAbort = oTmem + 4;
   static constexpr int kBytes = oAbort + 4;
@@ -86,6 +91,7 @@ finish_kernel(const float* __restrict__ dq_acc, T* __restrict__ dq, int64_t n) {
   }
 }
 
+
 template <typename T, int HD, bool CAUSAL>
 __global__ void __launch_bounds__(NTHREADS, 1)
 bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -94,18 +100,20 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
            float* __restrict__ dq_acc, T* __restrict__ dk, T* __restrict__ dv, int Tq, int M,
            float scale, float scale_log2) {
   using L = Smem<HD>;
+  constexpr bool kPairDq = (HD == 64);  // dQ per pair of query tiles (see header)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::oBar);
-  uint64_t* kv_full = bars + 0;
-  uint64_t* qdo_full = bars + 1;
-  uint64_t* qdo_empty = bars + 2;
-  uint64_t* s_full = bars + 3;
-  uint64_t* p_full = bars + 4;
-  uint64_t* mma2_done = bars + 5;
-  uint64_t* s_free = bars + 6;
-  uint64_t* drain = bars + 7;
+  uint64_t* kv_full = bars;
+  uint64_t* q_full = bars + 1;      // [2] Q_t and dO_t landed
+  uint64_t* q_empty = bars + 3;     // [2] stage free (MMAs reading it done)
+  uint64_t* s_full = bars + 5;      // [2] S^T, dP^T of the buffer computed
+  uint64_t* p_full = bars + 7;      // [2] P^T, dS^T of the buffer written (256 arrivals)
+  uint64_t* mma2_done = bars + 9;   // [2] dV, dK (and dQ) MMAs of the tile done
+  uint64_t* s_free = bars + 11;     // [2] dQ^T read out of the buffer (256 arrivals)
+  uint64_t* dq_free = bars + 13;    // pair dQ read out (256 arrivals)
+  uint64_t* drain = bars + 14;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::oTmem);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + L::oAbort);
 
@@ -117,7 +125,17 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
   const int n_iter = n_qt > i_begin ? n_qt - i_begin : 0;
 
   if (threadIdx.x == 0) {
-    for (int b = 0; b < 8; ++b) tc::mbar_init(bars + b, (b == 4 || b == 6) ? 128 : 1);
+    tc::mbar_init(kv_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      tc::mbar_init(q_full + b, 1);
+      tc::mbar_init(q_empty + b, 1);
+      tc::mbar_init(s_full + b, 1);
+      tc::mbar_init(p_full + b, NCOMPUTE);
+      tc::mbar_init(mma2_done + b, 1);
+      tc::mbar_init(s_free + b, NCOMPUTE);
+    }
+    tc::mbar_init(dq_free, NCOMPUTE);
+    tc::mbar_init(drain, 1);
     *abort = 0;
     tc::fence_barrier_init();
   }
@@ -126,31 +144,35 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t t_s = tmem, t_dp = tmem + 128, t_dv = tmem + 256, t_dk = tmem + 256 + HD;
+  const uint32_t t_dv = tmem + 256, t_dk = tmem + 256 + HD, t_dqp = tmem + 384;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0 && n_iter > 0) {
       tc::prefetch_tmap(&tm_q);
       tc::prefetch_tmap(&tm_do);
-      tc::mbar_expect_tx(kv_full, 2 * L::kTile);
+      tc::mbar_expect_tx(kv_full, 2 * L::kKV);
       for (int cb = 0; cb < HD / 64; ++cb) {
         tc::tma_load_3d(smem + L::oK + cb * BK * 128, &tm_k, kv_full, cb * 64, k0, bh);
         tc::tma_load_3d(smem + L::oV + cb * BK * 128, &tm_v, kv_full, cb * 64, k0, bh);
       }
       int issued = 0;
       for (int t = 0; t < n_iter; ++t) {
-        if (t > 0 && !tc::mbar_wait(qdo_empty, (t - 1) & 1, abort)) break;
+        const int b = t & 1;
+        if (t >= 2 && !tc::mbar_wait(q_empty + b, ((t - 2) >> 1) & 1, abort)) break;
         const int q0 = (i_begin + t) * BQ;
-        tc::mbar_expect_tx(qdo_full, 2 * L::kTile);
+        tc::mbar_expect_tx(q_full + b, 2 * L::kQ);
         for (int cb = 0; cb < HD / 64; ++cb) {
-          tc::tma_load_3d(smem + L::oQ + cb * BQ * 128, &tm_q, qdo_full, cb * 64, q0, bh);
-          tc::tma_load_3d(smem + L::oDO + cb * BQ * 128, &tm_do, qdo_full, cb * 64, q0, bh);
+          tc::tma_load_3d(smem + L::oQ + b * L::kQ + cb * BQ * 128, &tm_q, q_full + b, cb * 64,
+                          q0, bh);
+          tc::tma_load_3d(smem + L::oDO + b * L::kQ + cb * BQ * 128, &tm_do, q_full + b,
+                          cb * 64, q0, bh);
         }
         issued = t + 1;
       }
       tc::mbar_wait_drain(kv_full, 0);
-      if (issued > 0) tc::mbar_wait_drain(qdo_full, (issued - 1) & 1);
+      for (int t = issued > 2 ? issued - 2 : 0; t < issued; ++t)
+        tc::mbar_wait_drain(q_full + (t & 1), (t >> 1) & 1);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -158,54 +180,77 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       constexpr int ab = tc::AbFmt<T>::v;
       constexpr uint32_t id_s = tc::idesc_f16(BK, BQ, ab, 0, 0);    // S^T, dP^T
       constexpr uint32_t id_kv = tc::idesc_f16(BK, HD, ab, 0, 1);   // dV, dK
-      constexpr uint32_t id_q = tc::idesc_f16(BQ, HD, ab, 1, 1);    // dQ
+      constexpr uint32_t id_dqt = tc::idesc_f16(HD, BQ, ab, 1, 1);  // dQ^T (HD == 128)
+      constexpr uint32_t id_dqp = tc::idesc_f16(2 * BQ, HD, ab, 1, 1);  // pair dQ (HD == 64)
       const uint32_t a_k = tc::smem_u32(smem + L::oK), a_v = tc::smem_u32(smem + L::oV);
       const uint32_t a_q = tc::smem_u32(smem + L::oQ), a_do = tc::smem_u32(smem + L::oDO);
       const uint32_t a_p = tc::smem_u32(smem + L::oP), a_ds = tc::smem_u32(smem + L::oDS);
-      bool ok = tc::mbar_wait(kv_full, 0, abort);
-      for (int t = 0; ok && t < n_iter; ++t) {
-        if (!tc::mbar_wait(qdo_full, t & 1, abort)) break;
-        if (t > 0 && !tc::mbar_wait(s_free, (t - 1) & 1, abort)) break;
+      auto issue_s = [&](int t) -> bool {
+        const int b = t & 1;
+        if (!tc::mbar_wait(q_full + b, (t >> 1) & 1, abort)) return false;
+        if (!kPairDq && t >= 2 && !tc::mbar_wait(s_free + b, ((t - 2) >> 1) & 1, abort))
+          return false;
         tc::tc_fence_after();
+        const uint32_t ts = tmem + b * 128;
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t off = (kk / 4) * (128 * 128) + (kk % 4) * 32;
-          tc::mma_ss(t_s, tc::sw128_desc(a_k + off, 16, 1024), tc::sw128_desc(a_q + off, 16, 1024),
-                     id_s, kk > 0 ? 1u : 0u);
-          tc::mma_ss(t_dp, tc::sw128_desc(a_v + off, 16, 1024),
-                     tc::sw128_desc(a_do + off, 16, 1024), id_s, kk > 0 ? 1u : 0u);
+          const uint32_t off_a = (kk / 4) * (BK * 128) + (kk % 4) * 32;
+          const uint32_t off_b = b * L::kQ + (kk / 4) * (BQ * 128) + (kk % 4) * 32;
+          tc::mma_ss(ts, tc::sw128_desc(a_k + off_a, 16, 1024),
+                     tc::sw128_desc(a_q + off_b, 16, 1024), id_s, kk > 0 ? 1u : 0u);
+          tc::mma_ss(ts + 64, tc::sw128_desc(a_v + off_a, 16, 1024),
+                     tc::sw128_desc(a_do + off_b, 16, 1024), id_s, kk > 0 ? 1u : 0u);
         }
-        tc::mma_commit(s_full);
-        if (!tc::mbar_wait(p_full, t & 1, abort)) break;
+        tc::mma_commit(s_full + b);
+        return true;
+      };
+      bool ok = tc::mbar_wait(kv_full, 0, abort);
+      if (ok) ok = issue_s(0);
+      for (int t = 0; ok && t < n_iter; ++t) {
+        const int b = t & 1;
+        if (t + 1 < n_iter && !issue_s(t + 1)) break;
+        if (!tc::mbar_wait(p_full + b, (t >> 1) & 1, abort)) break;
         tc::tc_fence_after();
-        const uint32_t acc = t > 0 ? 1u : 0u;
+        const uint32_t a_pb = a_p + b * L::kP, a_dsb = a_ds + b * L::kP;
 #pragma unroll
         for (int kk = 0; kk < BQ / 16; ++kk) {
-          // contraction over queries: P^T / dS^T K-major, dO / Q MN-major
-          const uint32_t off_a = (kk / 4) * (BK * 128) + (kk % 4) * 32;
-          const uint32_t off_b = kk * 16 * 128;
-          tc::mma_ss(t_dv, tc::sw128_desc(a_p + off_a, 16, 1024),
-                     tc::sw128_desc(a_do + off_b, BQ * 128, 1024), id_kv, (acc | kk) ? 1u : 0u);
-          tc::mma_ss(t_dk, tc::sw128_desc(a_ds + off_a, 16, 1024),
-                     tc::sw128_desc(a_q + off_b, BQ * 128, 1024), id_kv, (acc | kk) ? 1u : 0u);
+          // contraction over the tile's queries: P^T / dS^T K-major, dO / Q MN-major
+          const uint32_t off_b = b * L::kQ + kk * 16 * 128;
+          const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
+          tc::mma_ss(t_dv, tc::sw128_desc(a_pb + kk * 32, 16, 1024),
+                     tc::sw128_desc(a_do + off_b, BQ * 128, 1024), id_kv, acc);
+          tc::mma_ss(t_dk, tc::sw128_desc(a_dsb + kk * 32, 16, 1024),
+                     tc::sw128_desc(a_q + off_b, BQ * 128, 1024), id_kv, acc);
         }
+        if constexpr (!kPairDq) {
+          // dQ^T = K^T dS^T over the keys, into this buffer's S^T columns
 #pragma unroll
-        for (int kk = 0; kk < BK / 16; ++kk) {
-          // contraction over keys: dS^T read as MN-major A, K as MN-major B
-          const uint32_t off = kk * 16 * 128;
-          tc::mma_ss(t_s, tc::sw128_desc(a_ds + off, BK * 128, 1024),
-                     tc::sw128_desc(a_k + off, BK * 128, 1024), id_q, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < BK / 16; ++kk)
+            tc::mma_ss(tmem + b * 128, tc::sw128_desc(a_k + kk * 2048, BK * 128, 1024),
+                       tc::sw128_desc(a_dsb + kk * 2048, BK * 128, 1024), id_dqt,
+                       kk > 0 ? 1u : 0u);
+        } else if ((t & 1) || t == n_iter - 1) {
+          // dQ for the pair (2p, 2p+1): both dS^T buffers as one M = 128 operand
+          const int p = t >> 1;
+          if (p > 0 && !tc::mbar_wait(dq_free, (p - 1) & 1, abort)) break;
+          tc::tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            tc::mma_ss(t_dqp, tc::sw128_desc(a_ds + kk * 2048, L::kP, 1024),
+                       tc::sw128_desc(a_k + kk * 2048, BK * 128, 1024), id_dqp,
+                       kk > 0 ? 1u : 0u);
         }
-        tc::mma_commit(mma2_done);
-        tc::mma_commit(qdo_empty);
+        tc::mma_commit(mma2_done + b);
+        tc::mma_commit(q_empty + b);
       }
       tc::mma_commit(drain);
       tc::mbar_wait_drain(drain, 0);
     }
   } else {
     // ------------------------------------------------------------ compute
+    const int grp = (warp - 2) >> 2;    // column half this warp handles
     const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;  // TMEM lane: key row (S^T, dV, dK) or query row (dQ)
+    const int r = quarter * 32 + lane;  // TMEM lane of this thread
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const int key = k0 + r;
     bool ok = true;
@@ -213,79 +258,110 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       return __all_sync(0xffffffffu, tc::mbar_wait(bar, parity, abort));
     };
     const uint32_t a_p = tc::smem_u32(smem + L::oP), a_ds = tc::smem_u32(smem + L::oDS);
+    const size_t row_base = (size_t)bh * Tq;
+
+    // dQ of finished work -> fp32 accumulator (pre-scaled).
+    auto readout = [&](int t) {
+      if constexpr (!kPairDq) {
+        // dQ^T of tile t: lane = head-dim index r, 32 query columns of this group
+        float v[32];
+        tc::tmem_ld32(tmem + (t & 1) * 128 + lane_off + grp * 32, v);
+        const int qb = (i_begin + t) * BQ + grp * 32;
+#pragma unroll
+        for (int e = 0; e < 32; ++e)
+          if (qb + e < Tq)
+            atomicAdd(dq_acc + (row_base + qb + e) * HD + r, v[e] * scale);
+        tc::tc_fence_before();
+        tc::mbar_arrive(s_free + (t & 1));
+      } else {
+        // pair dQ ending at tile t: lane = query row of the pair, 32 head dims
+        float v[32];
+        tc::tmem_ld32(t_dqp + lane_off + grp * 32, v);
+        const int q = (i_begin + (t & ~1)) * BQ + r;
+        if (q < Tq) {
+          float* dst = dq_acc + (row_base + q) * HD + grp * 32;
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            red_add_v4(dst + 4 * i, v[4 * i] * scale, v[4 * i + 1] * scale,
+                       v[4 * i + 2] * scale, v[4 * i + 3] * scale);
+        }
+        tc::tc_fence_before();
+        tc::mbar_arrive(dq_free);
+      }
+    };
+
     for (int t = 0; t < n_iter; ++t) {
+      const int b = t & 1;
       const int q0 = (i_begin + t) * BQ;
-      if (!wait(s_full, t & 1)) { ok = false; break; }
+      if (t >= 1) {
+        // The previous tile's MMAs are done: its dQ can be read out and the
+        // P^T / dS^T buffer this tile writes is free again.
+        if (!wait(mma2_done + ((t - 1) & 1), ((t - 1) >> 1) & 1)) { ok = false; break; }
+        tc::tc_fence_after();
+        if (!kPairDq) {
+          readout(t - 1);
+        } else if (!(t & 1)) {
+          readout(t - 1);  // the pair (t-2, t-1)
+        }
+      }
+      if (!wait(s_full + b, (t >> 1) & 1)) { ok = false; break; }
       tc::tc_fence_after();
+      float s[32], dp[32];
+      tc::tmem_ld32(tmem + b * 128 + lane_off + grp * 32, s);
+      tc::tmem_ld32(tmem + b * 128 + 64 + lane_off + grp * 32, dp);
       const bool diag = CAUSAL && (q0 < k0 + BK);
-#pragma unroll 1
-      for (int c = 0; c < BQ / 32; ++c) {
-        float s[32], dp[32];
-        tc::tmem_ld32(t_s + lane_off + c * 32, s);
-        tc::tmem_ld32(t_dp + lane_off + c * 32, dp);
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int qi = c * 32 + e;
-          // Row statistics straight from global memory: every lane reads
-          // the same address, so each is one broadcast load through L1.
-          const int q = q0 + qi;
-          const bool in = q < Tq;
-          const float lq = in ? __ldg(lse + (size_t)bh * Tq + q) * 1.4426950408889634f : 0.f;
-          const float zq = in ? __ldg(z + (size_t)bh * Tq + q) : 0.f;
-          float p = tc::ex2(s[e] * scale_log2 - lq);
-          if (!in || key >= M || (diag && q < key)) p = 0.f;
-          s[e] = p;                   // P^T
-          dp[e] = p * (dp[e] - zq);   // dS^T
-        }
-        // 32 query columns = 4 chunks of 8 in column block c/2
-        const uint32_t blk = (uint32_t)(c >> 1) * (BK * 128);
+      for (int e = 0; e < 32; ++e) {
+        // Row statistics straight from global memory: all lanes read the
+        // same address, one broadcast load through L1 each.
+        const int q = q0 + grp * 32 + e;
+        const bool in = q < Tq;
+        const float lq = in ? __ldg(lse + row_base + q) * 1.4426950408889634f : 0.f;
+        const float zq = in ? __ldg(z + row_base + q) : 0.f;
+        float p = tc::ex2(s[e] * scale_log2 - lq);
+        if (!in || key >= M || (diag && q < key)) p = 0.f;
+        s[e] = p;                   // P^T
+        dp[e] = p * (dp[e] - zq);   // dS^T
+      }
+      if (kPairDq && (t & 1) && t >= 3) {
+        // buffer b was last read by tile t-2's dV/dK MMAs (mma2_{t-2})
+        if (!wait(mma2_done + b, ((t - 2) >> 1) & 1)) { ok = false; break; }
+      }
+      const uint32_t pb = a_p + b * L::kP, db = a_ds + b * L::kP;
 #pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          const uint32_t ch = (uint32_t)((c & 1) * 4 + h);
-          const float* pe = s + h * 8;
-          const float* de = dp + h * 8;
-          tc::st_shared_v4(a_p + blk + tc::sw128_off(r, ch), tc::pack2<T>(pe[0], pe[1]),
-                           tc::pack2<T>(pe[2], pe[3]), tc::pack2<T>(pe[4], pe[5]),
-                           tc::pack2<T>(pe[6], pe[7]));
-          tc::st_shared_v4(a_ds + blk + tc::sw128_off(r, ch), tc::pack2<T>(de[0], de[1]),
-                           tc::pack2<T>(de[2], de[3]), tc::pack2<T>(de[4], de[5]),
-                           tc::pack2<T>(de[6], de[7]));
-        }
+      for (int h = 0; h < 4; ++h) {
+        const uint32_t off = tc::sw128_off(r, grp * 4 + h);
+        const float* pe = s + h * 8;
+        const float* de = dp + h * 8;
+        tc::st_shared_v4(pb + off, tc::pack2<T>(pe[0], pe[1]), tc::pack2<T>(pe[2], pe[3]),
+                         tc::pack2<T>(pe[4], pe[5]), tc::pack2<T>(pe[6], pe[7]));
+        tc::st_shared_v4(db + off, tc::pack2<T>(de[0], de[1]), tc::pack2<T>(de[2], de[3]),
+                         tc::pack2<T>(de[4], de[5]), tc::pack2<T>(de[6], de[7]));
       }
       tc::fence_proxy_async_smem();
       tc::tc_fence_before();
-      tc::mbar_arrive(p_full);
-      // dQ_i partial of this key tile -> fp32 accumulator
-      if (!wait(mma2_done, t & 1)) { ok = false; break; }
-      tc::tc_fence_after();
-      const int qrow = q0 + r;
-      float* dst = dq_acc + ((size_t)bh * Tq + (size_t)(qrow < Tq ? qrow : 0)) * HD;
-#pragma unroll 1
-      for (int c = 0; c < HD / 32; ++c) {
-        float v[32];
-        tc::tmem_ld32(t_s + lane_off + c * 32, v);
-        if (qrow < Tq) {
-#pragma unroll
-          for (int i = 0; i < 8; ++i)
-            red_add_v4(dst + c * 32 + 4 * i, v[4 * i] * scale, v[4 * i + 1] * scale,
-                       v[4 * i + 2] * scale, v[4 * i + 3] * scale);
-        }
-      }
-      tc::tc_fence_before();
-      tc::mbar_arrive(s_free);
+      tc::mbar_arrive(p_full + b);
     }
-    // ------------------------------------------------------------ dK, dV
+    // ------------------------------------------------------------ tail, dK, dV
+    if (ok && n_iter > 0) {
+      const int tl = n_iter - 1;
+      ok = wait(mma2_done + (tl & 1), (tl >> 1) & 1);
+      if (ok) {
+        tc::tc_fence_after();
+        readout(tl);  // last tile's dQ^T, or the last (possibly half) pair
+      }
+    }
     if (ok) {
       const bool store = key < M;
       const size_t base = ((size_t)bh * M + (store ? key : 0)) * HD;
 #pragma unroll 1
       for (int which = 0; which < 2; ++which) {
         T* out = which == 0 ? dv : dk;
+        if (out == nullptr) continue;
         const float mul = which == 0 ? 1.f : scale;
         const uint32_t col = which == 0 ? t_dv : t_dk;
-        if (out == nullptr) continue;
 #pragma unroll 1
-        for (int c = 0; c < HD / 32; ++c) {
+        for (int c = grp * (HD / 64); c < (grp + 1) * (HD / 64); ++c) {
           float v[32];
           if (n_iter > 0) {
             tc::tmem_ld32(col + lane_off + c * 32, v);
