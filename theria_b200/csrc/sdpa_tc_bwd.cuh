@@ -30,7 +30,8 @@ namespace tcbwd {
 constexpr int BK = 128;        // keys per CTA (M of S^T, dP^T, dV, dK)
 constexpr int BQ = 64;         // query rows per iteration (N of S^T, dP^T)
 constexpr int NCOMPUTE = 256;  // 8 compute warps: 2 groups x 4 TMEM lane quarters
-constexpr int NTHREADS = 64 + NCOMPUTE;
+constexpr int NDQ = 128;       // 4 warps that flush dQ (one per TMEM lane quarter)
+constexpr int NTHREADS = 64 + NCOMPUTE + NDQ;
 
 template <int HD>
 struct Smem {
@@ -132,9 +133,9 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       tc::mbar_init(s_full + b, 1);
       tc::mbar_init(p_full + b, NCOMPUTE);
       tc::mbar_init(mma2_done + b, 1);
-      tc::mbar_init(s_free + b, NCOMPUTE);
+      tc::mbar_init(s_free + b, NDQ);
     }
-    tc::mbar_init(dq_free, NCOMPUTE);
+    tc::mbar_init(dq_free, NDQ);
     tc::mbar_init(drain, 1);
     *abort = 0;
     tc::fence_barrier_init();
@@ -188,18 +189,26 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       auto issue_s = [&](int t) -> bool {
         const int b = t & 1;
         if (!tc::mbar_wait(q_full + b, (t >> 1) & 1, abort)) return false;
+        tc::tc_fence_after();
+        const uint32_t ts = tmem + b * 128;
+        // dP^T first: its columns are free as soon as the tile two back was
+        // consumed; S^T's columns may still hold that tile's dQ^T.
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off_a = (kk / 4) * (BK * 128) + (kk % 4) * 32;
+          const uint32_t off_b = b * L::kQ + (kk / 4) * (BQ * 128) + (kk % 4) * 32;
+          tc::mma_ss(ts + 64, tc::sw128_desc(a_v + off_a, 16, 1024),
+                     tc::sw128_desc(a_do + off_b, 16, 1024), id_s, kk > 0 ? 1u : 0u);
+        }
         if (!kPairDq && t >= 2 && !tc::mbar_wait(s_free + b, ((t - 2) >> 1) & 1, abort))
           return false;
         tc::tc_fence_after();
-        const uint32_t ts = tmem + b * 128;
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
           const uint32_t off_a = (kk / 4) * (BK * 128) + (kk % 4) * 32;
           const uint32_t off_b = b * L::kQ + (kk / 4) * (BQ * 128) + (kk % 4) * 32;
           tc::mma_ss(ts, tc::sw128_desc(a_k + off_a, 16, 1024),
                      tc::sw128_desc(a_q + off_b, 16, 1024), id_s, kk > 0 ? 1u : 0u);
-          tc::mma_ss(ts + 64, tc::sw128_desc(a_v + off_a, 16, 1024),
-                     tc::sw128_desc(a_do + off_b, 16, 1024), id_s, kk > 0 ? 1u : 0u);
         }
         tc::mma_commit(s_full + b);
         return true;
@@ -246,11 +255,13 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       tc::mma_commit(drain);
       tc::mbar_wait_drain(drain, 0);
     }
-  } else {
+  } else if (warp < 2 + NCOMPUTE / 32) {
     // ------------------------------------------------------------ compute
-    const int grp = (warp - 2) >> 2;    // column half this warp handles
+    // Warps 2..9: P^T and dS^T, then dK / dV at the end.  Group `grp`
+    // handles query columns [32 grp, 32 grp + 32) of each tile.
+    const int grp = (warp - 2) >> 2;
     const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;  // TMEM lane of this thread
+    const int r = quarter * 32 + lane;  // TMEM lane = key row
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const int key = k0 + r;
     bool ok = true;
@@ -259,50 +270,20 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
     };
     const uint32_t a_p = tc::smem_u32(smem + L::oP), a_ds = tc::smem_u32(smem + L::oDS);
     const size_t row_base = (size_t)bh * Tq;
-
-    // dQ of finished work -> fp32 accumulator (pre-scaled).
-    auto readout = [&](int t) {
-      if constexpr (!kPairDq) {
-        // dQ^T of tile t: lane = head-dim index r, 32 query columns of this group
-        float v[32];
-        tc::tmem_ld32(tmem + (t & 1) * 128 + lane_off + grp * 32, v);
-        const int qb = (i_begin + t) * BQ + grp * 32;
-#pragma unroll
-        for (int e = 0; e < 32; ++e)
-          if (qb + e < Tq)
-            atomicAdd(dq_acc + (row_base + qb + e) * HD + r, v[e] * scale);
-        tc::tc_fence_before();
-        tc::mbar_arrive(s_free + (t & 1));
-      } else {
-        // pair dQ ending at tile t: lane = query row of the pair, 32 head dims
-        float v[32];
-        tc::tmem_ld32(t_dqp + lane_off + grp * 32, v);
-        const int q = (i_begin + (t & ~1)) * BQ + r;
-        if (q < Tq) {
-          float* dst = dq_acc + (row_base + q) * HD + grp * 32;
-#pragma unroll
-          for (int i = 0; i < 8; ++i)
-            red_add_v4(dst + 4 * i, v[4 * i] * scale, v[4 * i + 1] * scale,
-                       v[4 * i + 2] * scale, v[4 * i + 3] * scale);
-        }
-        tc::tc_fence_before();
-        tc::mbar_arrive(dq_free);
-      }
-    };
-
     for (int t = 0; t < n_iter; ++t) {
       const int b = t & 1;
       const int q0 = (i_begin + t) * BQ;
-      if (t >= 1) {
-        // The previous tile's MMAs are done: its dQ can be read out and the
-        // P^T / dS^T buffer this tile writes is free again.
-        if (!wait(mma2_done + ((t - 1) & 1), ((t - 1) >> 1) & 1)) { ok = false; break; }
-        tc::tc_fence_after();
-        if (!kPairDq) {
-          readout(t - 1);
-        } else if (!(t & 1)) {
-          readout(t - 1);  // the pair (t-2, t-1)
-        }
+      // Row statistics of this group's 32 queries: one load per lane, then
+      // broadcast by shuffles.
+      const int ql = q0 + grp * 32 + lane;
+      const float my_l = ql < Tq ? __ldg(lse + row_base + ql) * 1.4426950408889634f : INFINITY;
+      const float my_z = ql < Tq ? __ldg(z + row_base + ql) : 0.f;
+      // P^T / dS^T buffer b is free once the MMAs that read it are done:
+      // tile t-2's dV/dK (and dQ); with paired dQ, an even tile's buffer is
+      // also read by the pair MMA issued with tile t-1.
+      if (t >= 2) {
+        const int tw = (kPairDq && !(t & 1)) ? t - 1 : t - 2;
+        if (!wait(mma2_done + (tw & 1), (tw >> 1) & 1)) { ok = false; break; }
       }
       if (!wait(s_full + b, (t >> 1) & 1)) { ok = false; break; }
       tc::tc_fence_after();
@@ -312,20 +293,12 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       const bool diag = CAUSAL && (q0 < k0 + BK);
 #pragma unroll
       for (int e = 0; e < 32; ++e) {
-        // Row statistics straight from global memory: all lanes read the
-        // same address, one broadcast load through L1 each.
-        const int q = q0 + grp * 32 + e;
-        const bool in = q < Tq;
-        const float lq = in ? __ldg(lse + row_base + q) * 1.4426950408889634f : 0.f;
-        const float zq = in ? __ldg(z + row_base + q) : 0.f;
-        float p = tc::ex2(s[e] * scale_log2 - lq);
-        if (!in || key >= M || (diag && q < key)) p = 0.f;
+        const float lq = __shfl_sync(0xffffffffu, my_l, e);
+        const float zq = __shfl_sync(0xffffffffu, my_z, e);
+        float p = tc::ex2(s[e] * scale_log2 - lq);  // rows past the end: lq = +inf -> 0
+        if (key >= M || (diag && q0 + grp * 32 + e < key)) p = 0.f;
         s[e] = p;                   // P^T
         dp[e] = p * (dp[e] - zq);   // dS^T
-      }
-      if (kPairDq && (t & 1) && t >= 3) {
-        // buffer b was last read by tile t-2's dV/dK MMAs (mma2_{t-2})
-        if (!wait(mma2_done + b, ((t - 2) >> 1) & 1)) { ok = false; break; }
       }
       const uint32_t pb = a_p + b * L::kP, db = a_ds + b * L::kP;
 #pragma unroll
@@ -342,14 +315,11 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       tc::tc_fence_before();
       tc::mbar_arrive(p_full + b);
     }
-    // ------------------------------------------------------------ tail, dK, dV
+    // ------------------------------------------------------------ dK, dV
     if (ok && n_iter > 0) {
       const int tl = n_iter - 1;
       ok = wait(mma2_done + (tl & 1), (tl >> 1) & 1);
-      if (ok) {
-        tc::tc_fence_after();
-        readout(tl);  // last tile's dQ^T, or the last (possibly half) pair
-      }
+      if (ok) tc::tc_fence_after();
     }
     if (ok) {
       const bool store = key < M;
@@ -380,6 +350,55 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
                                tc::pack2<T>(e[6] * mul, e[7] * mul));
           }
         }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ dQ flush
+    // Warps 10..13: read each finished dQ out of TMEM and add it (scaled)
+    // into the fp32 accumulator, concurrently with the next tile's compute.
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const size_t row_base = (size_t)bh * Tq;
+    auto wait = [&](uint64_t* bar, uint32_t parity) {
+      return __all_sync(0xffffffffu, tc::mbar_wait(bar, parity, abort));
+    };
+    for (int t = 0; t < n_iter; ++t) {
+      if (kPairDq && !(t & 1) && t != n_iter - 1) continue;  // pairs finish on odd tiles
+      if (!wait(mma2_done + (t & 1), (t >> 1) & 1)) break;
+      tc::tc_fence_after();
+      if constexpr (!kPairDq) {
+        // dQ^T of tile t: lane = head-dim index r, 64 query columns
+        const int qb = (i_begin + t) * BQ;
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          float v[32];
+          tc::tmem_ld32(tmem + (t & 1) * 128 + lane_off + c * 32, v);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int q = qb + c * 32 + e;
+            if (q < Tq) atomicAdd(dq_acc + (row_base + q) * HD + r, v[e] * scale);
+          }
+        }
+        tc::tc_fence_before();
+        tc::mbar_arrive(s_free + (t & 1));
+      } else {
+        // dQ of the pair ending at tile t: lane = query row, 64 head dims
+        const int q = (i_begin + (t & ~1)) * BQ + r;
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          float v[32];
+          tc::tmem_ld32(t_dqp + lane_off + c * 32, v);
+          if (q < Tq) {
+            float* dst = dq_acc + (row_base + q) * HD + c * 32;
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              red_add_v4(dst + 4 * i, v[4 * i] * scale, v[4 * i + 1] * scale,
+                         v[4 * i + 2] * scale, v[4 * i + 3] * scale);
+          }
+        }
+        tc::tc_fence_before();
+        tc::mbar_arrive(dq_free);
       }
     }
   }
