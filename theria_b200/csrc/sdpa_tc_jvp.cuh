@@ -1,0 +1,311 @@
+// Tensor-core (tcgen05) frozen-stats JVP for bf16/fp16, head dim 64 or 128,
+// and the first pass of the HVP (same kernel with W).
+//
+// One CTA owns 128 query rows of one (batch, head); P is rebuilt exactly
+// from the forward's LSE, so there is no online rescaling.  Per key tile j:
+//   S   = Q K^T                       (tcgen05 -> TMEM)
+//   Sd' = tQ K^T + Q tK^T             (tcgen05 -> TMEM, one accumulator)
+//   P   = exp(s S - LSE),  U = P * (s Sd')         (CUDA cores, 16-bit tiles)
+//   OA += U V,   [OP | OT] += P [V | tV]           (tcgen05; V and tV sit
+//                                                   side by side in smem, so
+//                                                   one N = 2D MMA covers both)
+//   c  += rowsum(U)
+// and at the end Odot = OA - c OP + OT.  With W (HVP pass 1) the kernel also
+// stores the row terms c, z = rowsum(W OP), zdot = rowsum(W Odot).
+// Key tile BN = 128 for D = 64 and 64 for D = 128, so that
+// TMEM = S (BN) + Sd (BN) + OA (D) + [OP|OT] (2D) fits in 512 columns.
+// Warp roles: 0 TMA, 1 MMA issuer + TMEM owner, 2..9 compute (two groups
+// splitting each tile's key columns, four TMEM lane quarters each).
+#pragma once
+
+#include "tc_common.cuh"
+
+namespace theria {
+namespace tcjvp {
+
+constexpr int BM = 128;
+constexpr int NCOMPUTE = 256;
+constexpr int NTHREADS = 64 + NCOMPUTE;
+
+template <int HD>
+struct Cfg {
+  static constexpr int BN = HD == 128 ? 64 : 128;
+  static constexpr int kQ = BM * HD * 2;
+  static constexpr int kKV = BN * HD * 2;
+  static constexpr int kP = BM * BN * 2;
+  static constexpr int oQ = 0;
+  static constexpr int oTQ = oQ + kQ;
+  static constexpr int oK = oTQ + kQ;
+  static constexpr int oTK = oK + kKV;
+  static constexpr int oV = oTK + kKV;
+  static constexpr int oTV = oV + kKV;  // directly after V: [V | tV] is one B operand
+  static constexpr int oP = oTV + kKV;
+  static constexpr int oU = oP + kP;
+  static constexpr int oStat = oU + kP;  // 3 x 128 floats: c, z, zdot partial sums
+  static constexpr int oBar = oStat + 3 * BM * 4;
+  // q_full, kt_full, kt_empty, vt_full, vt_empty, s_full, s_free, p_full,
+  // pv_done, c_ready, w_ready, drain
+  static constexpr int nBar = 12;
+  static constexpr int oTmem = oBar + nBar * 8;
+  static constexpr int oAbort = oTmem + 4;
+  static constexpr int kAlloc = oAbort + 4 + 1024;
+  // TMEM columns
+  static constexpr int tS = 0, tSd = BN, tOA = 2 * BN, tOP = 2 * BN + HD, tOT = 2 * BN + 2 * HD;
+};
+
+template <typename T, int HD, bool CAUSAL, bool WITH_W>
+__global__ void __launch_bounds__(NTHREADS, 1)
+jvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_tq,
+           const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_tk,
+           const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_tv,
+           const float* __restrict__ lse, const T* __restrict__ w, T* __restrict__ o_tan,
+           float* __restrict__ stats, int64_t n_rows_total, int Tq, int M, float scale,
+           float scale_log2) {
+  using C = Cfg<HD>;
+  constexpr int BN = C::BN;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::oBar);
+  uint64_t *q_full = bars, *kt_full = bars + 1, *kt_empty = bars + 2, *vt_full = bars + 3,
+           *vt_empty = bars + 4, *s_full = bars + 5, *s_free = bars + 6, *p_full = bars + 7,
+           *pv_done = bars + 8, *c_ready = bars + 9, *w_ready = bars + 10, *drain = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::oTmem);
+  volatile int* abort = reinterpret_cast<volatile int*>(smem + C::oAbort);
+  float* stat_s = reinterpret_cast<float*>(smem + C::oStat);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.y;
+  const int qt = CAUSAL ? (gridDim.x - 1 - blockIdx.x) : blockIdx.x;
+  const int q0 = qt * BM;
+  int n_tiles = (M + BN - 1) / BN;
+  if (CAUSAL) n_tiles = min(n_tiles, (q0 + BM - 1) / BN + 1);
+
+  if (threadIdx.x == 0) {
+    for (int b = 0; b < C::nBar; ++b) {
+      const bool many = (bars + b == s_free) || (bars + b == p_full) || (bars + b == c_ready) ||
+                        (bars + b == w_ready);
+      tc::mbar_init(bars + b, many ? NCOMPUTE : 1);
+    }
+    *abort = 0;
+    tc::fence_barrier_init();
+  }
+  for (int i = threadIdx.x; i < 3 * BM; i += blockDim.x) stat_s[i] = 0.f;
+  if (warp == 1) tc::tmem_alloc(tmem_slot, 512);
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tc::mbar_expect_tx(q_full, 2 * C::kQ);
+      for (int cb = 0; cb < HD / 64; ++cb) {
+        tc::tma_load_3d(smem + C::oQ + cb * BM * 128, &tm_q, q_full, cb * 64, q0, bh);
+        tc::tma_load_3d(smem + C::oTQ + cb * BM * 128, &tm_tq, q_full, cb * 64, q0, bh);
+      }
+      int issued = 0;
+      for (int j = 0; j < n_tiles; ++j) {
+        if (j >= 1 && !tc::mbar_wait(kt_empty, (j - 1) & 1, abort)) break;
+        tc::mbar_expect_tx(kt_full, 2 * C::kKV);
+        for (int cb = 0; cb < HD / 64; ++cb) {
+          tc::tma_load_3d(smem + C::oK + cb * BN * 128, &tm_k, kt_full, cb * 64, j * BN, bh);
+          tc::tma_load_3d(smem + C::oTK + cb * BN * 128, &tm_tk, kt_full, cb * 64, j * BN, bh);
+        }
+        if (j >= 1 && !tc::mbar_wait(vt_empty, (j - 1) & 1, abort)) { issued = -(j + 1); break; }
+        tc::mbar_expect_tx(vt_full, 2 * C::kKV);
+        for (int cb = 0; cb < HD / 64; ++cb) {
+          tc::tma_load_3d(smem + C::oV + cb * BN * 128, &tm_v, vt_full, cb * 64, j * BN, bh);
+          tc::tma_load_3d(smem + C::oTV + cb * BN * 128, &tm_tv, vt_full, cb * 64, j * BN, bh);
+        }
+        issued = j + 1;
+      }
+      tc::mbar_wait_drain(q_full, 0);
+      if (issued > 0) {
+        tc::mbar_wait_drain(kt_full, (issued - 1) & 1);
+        tc::mbar_wait_drain(vt_full, (issued - 1) & 1);
+      } else if (issued < 0) {  // K/tK of tile -issued-1 went out, V/tV did not
+        tc::mbar_wait_drain(kt_full, (-issued - 1) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr int ab = tc::AbFmt<T>::v;
+      constexpr uint32_t id_s = tc::idesc_f16(BM, BN, ab, 0, 0);
+      constexpr uint32_t id_a = tc::idesc_f16(BM, HD, ab, 0, 1);
+      constexpr uint32_t id_pt = tc::idesc_f16(BM, 2 * HD, ab, 0, 1);
+      const uint32_t a_q = tc::smem_u32(smem + C::oQ), a_tq = tc::smem_u32(smem + C::oTQ);
+      const uint32_t a_k = tc::smem_u32(smem + C::oK), a_tk = tc::smem_u32(smem + C::oTK);
+      const uint32_t a_v = tc::smem_u32(smem + C::oV);
+      const uint32_t a_p = tc::smem_u32(smem + C::oP), a_u = tc::smem_u32(smem + C::oU);
+      bool ok = tc::mbar_wait(q_full, 0, abort);
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        if (!tc::mbar_wait(kt_full, j & 1, abort)) break;
+        if (j >= 1 && !tc::mbar_wait(s_free, (j - 1) & 1, abort)) break;
+        tc::tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t oq = (kk / 4) * (BM * 128) + (kk % 4) * 32;
+          const uint32_t ok_ = (kk / 4) * (BN * 128) + (kk % 4) * 32;
+          const uint32_t acc = kk > 0 ? 1u : 0u;
+          tc::mma_ss(tmem + C::tS, tc::sw128_desc(a_q + oq, 16, 1024),
+                     tc::sw128_desc(a_k + ok_, 16, 1024), id_s, acc);
+          tc::mma_ss(tmem + C::tSd, tc::sw128_desc(a_tq + oq, 16, 1024),
+                     tc::sw128_desc(a_k + ok_, 16, 1024), id_s, acc);
+          tc::mma_ss(tmem + C::tSd, tc::sw128_desc(a_q + oq, 16, 1024),
+                     tc::sw128_desc(a_tk + ok_, 16, 1024), id_s, 1u);
+        }
+        tc::mma_commit(s_full);
+        tc::mma_commit(kt_empty);
+        if (!tc::mbar_wait(p_full, j & 1, abort)) break;
+        if (!tc::mbar_wait(vt_full, j & 1, abort)) break;
+        tc::tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const uint32_t oa = (kk / 4) * (BM * 128) + (kk % 4) * 32;
+          const uint32_t ob = kk * 16 * 128;
+          const uint32_t acc = (j > 0 || kk > 0) ? 1u : 0u;
+          tc::mma_ss(tmem + C::tOA, tc::sw128_desc(a_u + oa, 16, 1024),
+                     tc::sw128_desc(a_v + ob, BN * 128, 1024), id_a, acc);
+          tc::mma_ss(tmem + C::tOP, tc::sw128_desc(a_p + oa, 16, 1024),
+                     tc::sw128_desc(a_v + ob, BN * 128, 1024), id_pt, acc);
+        }
+        tc::mma_commit(pv_done);
+        tc::mma_commit(vt_empty);
+      }
+      tc::mma_commit(drain);
+      tc::mbar_wait_drain(drain, 0);
+    }
+  } else {
+    // ------------------------------------------------------------ compute
+    constexpr int HALF = BN / 2;  // key columns per group
+    const int grp = (warp - 2) >> 2;
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;  // TMEM lane = query row in tile
+    const int row = q0 + r;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const bool row_ok = row < Tq;
+    const float lse2 = row_ok ? lse[(size_t)bh * Tq + row] * 1.4426950408889634f : INFINITY;
+    bool ok = true;
+    auto wait = [&](uint64_t* bar, uint32_t parity) {
+      return __all_sync(0xffffffffu, tc::mbar_wait(bar, parity, abort));
+    };
+    const uint32_t a_p = tc::smem_u32(smem + C::oP), a_u = tc::smem_u32(smem + C::oU);
+    float c_acc = 0.f;
+    for (int j = 0; j < n_tiles; ++j) {
+      if (!wait(s_full, j & 1)) { ok = false; break; }
+      tc::tc_fence_after();
+      float sv[HALF], sd[HALF];
+#pragma unroll
+      for (int c = 0; c < HALF / 32; ++c) {
+        float a[32], b[32];
+        tc::tmem_ld32(tmem + C::tS + lane_off + grp * HALF + c * 32, a);
+        tc::tmem_ld32(tmem + C::tSd + lane_off + grp * HALF + c * 32, b);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          sv[c * 32 + e] = a[e];
+          sd[c * 32 + e] = b[e];
+        }
+      }
+      tc::tc_fence_before();
+      tc::mbar_arrive(s_free);  // S / Sd columns may be overwritten by tile j+1
+      const int col0 = j * BN + grp * HALF;
+#pragma unroll
+      for (int e = 0; e < HALF; ++e) {
+        const int col = col0 + e;
+        const bool valid = col < M && (!CAUSAL || col <= row);
+        const float p = valid ? tc::ex2(sv[e] * scale_log2 - lse2) : 0.f;
+        const float u = p * (sd[e] * scale);
+        c_acc += u;
+        sv[e] = p;
+        sd[e] = u;
+      }
+      // P / U tiles were read by tile j-1's MMAs.
+      if (j >= 1 && !wait(pv_done, (j - 1) & 1)) { ok = false; break; }
+#pragma unroll
+      for (int h = 0; h < HALF / 8; ++h) {
+        const int colt = grp * HALF + h * 8;  // column within the tile
+        const uint32_t off = (uint32_t)(colt / 64) * (BM * 128) + tc::sw128_off(r, (colt % 64) / 8);
+        const float* pe = sv + h * 8;
+        const float* ue = sd + h * 8;
+        tc::st_shared_v4(a_p + off, tc::pack2<T>(pe[0], pe[1]), tc::pack2<T>(pe[2], pe[3]),
+                         tc::pack2<T>(pe[4], pe[5]), tc::pack2<T>(pe[6], pe[7]));
+        tc::st_shared_v4(a_u + off, tc::pack2<T>(ue[0], ue[1]), tc::pack2<T>(ue[2], ue[3]),
+                         tc::pack2<T>(ue[4], ue[5]), tc::pack2<T>(ue[6], ue[7]));
+      }
+      tc::fence_proxy_async_smem();
+      tc::tc_fence_before();
+      tc::mbar_arrive(p_full);
+    }
+    // ------------------------------------------------------------ epilogue
+    // c = rowsum(P Sd) over both groups' columns.
+    atomicAdd(stat_s + r, c_acc);
+    tc::mbar_arrive(c_ready);
+    if (ok) ok = wait(c_ready, 0);
+    if (ok) ok = wait(pv_done, (n_tiles - 1) & 1);
+    if (ok) {
+      tc::tc_fence_after();
+      const float c = stat_s[r];
+      const size_t base = ((size_t)bh * Tq + (size_t)(row_ok ? row : 0)) * HD;
+      float zp = 0.f, zdp = 0.f;
+#pragma unroll 1
+      for (int cc = grp * (HD / 64); cc < (grp + 1) * (HD / 64); ++cc) {
+        float oa[32], op[32], ot[32];
+        tc::tmem_ld32(tmem + C::tOA + lane_off + cc * 32, oa);
+        tc::tmem_ld32(tmem + C::tOP + lane_off + cc * 32, op);
+        tc::tmem_ld32(tmem + C::tOT + lane_off + cc * 32, ot);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) oa[e] = oa[e] - c * op[e] + ot[e];  // Odot
+        if (!row_ok) continue;
+        if (WITH_W) {
+          const uint4* w4 = reinterpret_cast<const uint4*>(w + base + cc * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const uint4 pk = w4[i];
+            const uint32_t wv[4] = {pk.x, pk.y, pk.z, pk.w};
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+              const T* two = reinterpret_cast<const T*>(&wv[h]);
+              const float w0 = to_f32<T>(two[0]), w1 = to_f32<T>(two[1]);
+              const int e = i * 8 + h * 2;
+              zp += w0 * op[e] + w1 * op[e + 1];
+              zdp += w0 * oa[e] + w1 * oa[e + 1];
+            }
+          }
+        }
+        if (o_tan != nullptr) {
+          uint4* d4 = reinterpret_cast<uint4*>(o_tan + base + cc * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float* e = oa + 8 * i;
+            d4[i] = make_uint4(tc::pack2<T>(e[0], e[1]), tc::pack2<T>(e[2], e[3]),
+                               tc::pack2<T>(e[4], e[5]), tc::pack2<T>(e[6], e[7]));
+          }
+        }
+      }
+      if (WITH_W) {
+        atomicAdd(stat_s + BM + r, zp);
+        atomicAdd(stat_s + 2 * BM + r, zdp);
+        tc::mbar_arrive(w_ready);
+        if (wait(w_ready, 0) && grp == 0 && row_ok) {
+          const int64_t gr = (int64_t)bh * Tq + row;
+          stats[gr] = c;
+          stats[n_rows_total + gr] = stat_s[BM + r];
+          stats[2 * n_rows_total + gr] = stat_s[2 * BM + r];
+        }
+      }
+    }
+  }
+  // ------------------------------------------------------------ teardown
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace tcjvp
+}  // namespace theria

@@ -5,6 +5,7 @@
 // workspace carving and kernel selection for each entry point.
 #include <algorithm>
 #include <cstdio>
+#include <type_traits>
 #include <initializer_list>
 #include <mutex>
 
@@ -12,6 +13,7 @@
 #include "sdpa_simt.cuh"
 #include "sdpa_tc_bwd.cuh"
 #include "sdpa_tc_fwd.cuh"
+#include "sdpa_tc_jvp.cuh"
 #include "tc_host.cuh"
 
 namespace theria {
@@ -112,10 +114,28 @@ int simt_jvp(const void* q, const void* k, const void* v, const void* tq, const 
 }
 
 template <typename T>
+int tc_jvp(const void* q, const void* k, const void* v, const void* tq, const void* tk,
+           const void* tv, const void* w, const float* lse, void* o_tan, float* stats,
+           const Shape& s, int dtype, cudaStream_t st);
+bool use_tc(int dtype, const Shape& s, std::initializer_list<const void*> ptrs);
+
+template <typename T> constexpr int dtype_of() {
+  return std::is_same<T, float>::value ? THERIA_F32
+         : std::is_same<T, __half>::value ? THERIA_F16 : THERIA_BF16;
+}
+
+template <typename T>
 int simt_hvp(const void* q, const void* k, const void* v, const void* w, const float* lse,
              const void* tq, const void* tk, const void* tv, void* hq, void* hk, void* hv,
              void* o_tan, float* stats, const Shape& s, cudaStream_t st) {
-  if (int e = simt_jvp<T>(q, k, v, tq, tk, tv, w, lse, o_tan, stats, s, st)) return e;
+  int e1 = -1;
+  if constexpr (!std::is_same<T, float>::value) {
+    if (use_tc(dtype_of<T>(), s, {q, k, v, tq, tk, tv, w, o_tan}))
+      e1 = tc_jvp<T>(q, k, v, tq, tk, tv, w, lse, o_tan, stats, s, dtype_of<T>(), st);
+  }
+  if (e1 > 0) return e1;
+  if (e1 < 0)
+    if (int e = simt_jvp<T>(q, k, v, tq, tk, tv, w, lse, o_tan, stats, s, st)) return e;
   if (hq != nullptr) {
     size_t sm = (4 * tile_floats(s.D) + simt::WARPS * 3 * s.D) * sizeof(float);
     auto kern = simt::hq_row_kernel<T>;
@@ -233,6 +253,45 @@ int tc_bwd(const void* q, const void* k, const void* v, const void* o, int o_dty
   return THERIA_OK;
 }
 
+template <typename T, int HD, bool CAUSAL, bool W>
+int tc_jvp_launch(const CUtensorMap* m, const float* lse, const void* w, void* o_tan,
+                  float* stats, const Shape& s, cudaStream_t st) {
+  using C = tcjvp::Cfg<HD>;
+  auto kern = tcjvp::jvp_kernel<T, HD, CAUSAL, W>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kAlloc);
+  dim3 grid((unsigned)((s.T + tcjvp::BM - 1) / tcjvp::BM), (unsigned)(s.B * s.H));
+  kern<<<grid, tcjvp::NTHREADS, C::kAlloc, st>>>(m[0], m[1], m[2], m[3], m[4], m[5], lse,
+                                                 (const T*)w, (T*)o_tan, stats,
+                                                 s.B * s.H * s.T, (int)s.T, (int)s.M, s.scale,
+                                                 s.scale * 1.4426950408889634f);
+  return launch_status();
+}
+
+// Tensor-core JVP (w == nullptr) or HVP pass 1 (row terms into `stats`);
+// -1 when no TMA descriptor fits.
+template <typename T>
+int tc_jvp(const void* q, const void* k, const void* v, const void* tq, const void* tk,
+           const void* tv, const void* w, const float* lse, void* o_tan, float* stats,
+           const Shape& s, int dtype, cudaStream_t st) {
+  CUtensorMap m[6];
+  const int64_t bh = s.B * s.H;
+  const uint32_t bn = s.D == 128 ? tcjvp::Cfg<128>::BN : tcjvp::Cfg<64>::BN;
+  const void* src[6] = {q, tq, k, tk, v, tv};
+  for (int i = 0; i < 6; ++i)
+    if (!tc::make_map_3d(&m[i], src[i], dtype, bh, i < 2 ? s.T : s.M, s.D,
+                         i < 2 ? (uint32_t)tcjvp::BM : bn))
+      return -1;
+  const bool hw = w != nullptr;
+#define THERIA_JVP(HD, C, W) tc_jvp_launch<T, HD, C, W>(m, lse, w, o_tan, stats, s, st)
+  if (s.D == 64) {
+    if (s.causal) return hw ? THERIA_JVP(64, true, true) : THERIA_JVP(64, true, false);
+    return hw ? THERIA_JVP(64, false, true) : THERIA_JVP(64, false, false);
+  }
+  if (s.causal) return hw ? THERIA_JVP(128, true, true) : THERIA_JVP(128, true, false);
+  return hw ? THERIA_JVP(128, false, true) : THERIA_JVP(128, false, false);
+#undef THERIA_JVP
+}
+
 bool use_tc(int dtype, const Shape& s, std::initializer_list<const void*> ptrs) {
   if (!tc::tc_eligible(dtype, s.T, s.M, s.D, s.B * s.H)) return false;
   for (const void* p : ptrs)
@@ -337,6 +396,13 @@ int theria_sdpa_jvp(const void* q, const void* k, const void* v, const void* tq,
   if (!q || !k || !v || !tq || !tk || !tv || !lse || !o_tan) return THERIA_ERR_INVALID_ARG;
   Shape s{B, H, T, M, D, scale, causal ? 1 : 0};
   cudaStream_t st = (cudaStream_t)stream;
+  if (use_tc(dtype, s, {q, k, v, tq, tk, tv, o_tan})) {
+    int e = dtype == THERIA_BF16
+                ? tc_jvp<__nv_bfloat16>(q, k, v, tq, tk, tv, nullptr, lse, o_tan, nullptr, s,
+                                        dtype, st)
+                : tc_jvp<__half>(q, k, v, tq, tk, tv, nullptr, lse, o_tan, nullptr, s, dtype, st);
+    if (e >= 0) return e;
+  }
   return THERIA_DISPATCH(dtype, simt_jvp, q, k, v, tq, tk, tv, nullptr, lse, o_tan, nullptr, s,
                          st);
 }
