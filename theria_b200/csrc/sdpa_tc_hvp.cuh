@@ -1,0 +1,369 @@
+// Tensor-core (tcgen05) HVP backward pass for bf16/fp16, head dim 64 or 128.
+//
+// Hessian-vector product of L = <O, W> along u = (tQ, tK, tV), given the
+// forward LSE and the row terms of pass 1 (c = rowsum(P Sdot),
+// z = rowsum(W O), zdot = rowsum(W Odot); see sdpa_tc_jvp.cuh).
+// One CTA per (128-key tile, batch*head), looping over 64-row query tiles:
+//   S^T  = K Q^T,   Sd'^T = K tQ^T + tK Q^T,   dP^T = V W^T,   dPd^T = tV W^T
+//   P = exp(s S - LSE), Pd = P (s Sd' - c), dS = P (dP - z),
+//   dSd = Pd (dP - z) + P (dPd - zdot)                     (CUDA cores)
+//   hK += dSd^T Q + dS^T tQ,   hV += Pd^T W                 (TMEM accumulators)
+//   hQ  = dSd K + dS tK   -> fp32 accumulator via global reductions
+// hQ is formed like dQ in the backward: for D = 128 as hQ^T (M = D lanes)
+// over the S^T columns once read, for D = 64 per pair of query tiles
+// (M = 128 query rows) in its own columns.
+// TMEM: S^T [0,64), Sd^T [64,128), dP^T [128,192), dPd^T [192,256),
+// hV [256, 256+D), hK [256+D, 256+2D), pair hQ [384, 448) for D = 64.
+// Warp roles: 0 TMA, 1 MMA issuer + TMEM owner, 2..9 compute, 10..13 hQ
+// flush.
+#pragma once
+
+#include "sdpa_tc_bwd.cuh"
+
+namespace theria {
+namespace tchvp {
+
+constexpr int BK = 128, BQ = 64;
+constexpr int NCOMPUTE = 256, NDQ = 128;
+constexpr int NTHREADS = 64 + NCOMPUTE + NDQ;
+
+template <int HD>
+struct Cfg {
+  static constexpr int ST = HD == 64 ? 2 : 1;  // Q/tQ/W ring depth (smem allows 2 at D=64)
+  static constexpr int kKV = BK * HD * 2;
+  static constexpr int kQ = BQ * HD * 2;
+  static constexpr int kP = BK * BQ * 2;
+  static constexpr int oK = 0, oV = kKV, oTK = 2 * kKV, oTV = 3 * kKV;
+  static constexpr int oQ = 4 * kKV;             // stage s: Q, tQ, W at oQ + s*3*kQ
+  static constexpr int oPd = oQ + ST * 3 * kQ;   // Pd^T [key][q]
+  static constexpr int NB = HD == 64 ? 2 : 1;   // dS/dSd buffers (2: pair operand)
+  static constexpr int oDS = oPd + kP;           // dS^T  x NB (adjacent)
+  static constexpr int oDSd = oDS + NB * kP;     // dSd^T x NB (adjacent)
+  static constexpr int oBar = oDSd + NB * kP;
+  // kv_full, q_full[2], q_empty[2], s_full, s_read, p_full, mma2_done[2],
+  // hq_free, drain
+  static constexpr int nBar = 12;
+  static constexpr int oTmem = oBar + nBar * 8;
+  static constexpr int oAbort = oTmem + 4;
+  static constexpr int kAlloc = oAbort + 4 + 1024;
+};
+
+template <typename T, int HD, bool CAUSAL>
+__global__ void __launch_bounds__(NTHREADS, 1)
+hvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_tq,
+           const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_k,
+           const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_tk,
+           const __grid_constant__ CUtensorMap tm_tv, const float* __restrict__ lse,
+           const float* __restrict__ stats, int64_t n_rows_total, float* __restrict__ hq_acc,
+           T* __restrict__ hk, T* __restrict__ hv, int Tq, int M, float scale,
+           float scale_log2) {
+  using C = Cfg<HD>;
+  constexpr bool kPair = (HD == 64);
+  constexpr int ST = C::ST;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::oBar);
+  uint64_t *kv_full = bars, *q_full = bars + 1, *q_empty = bars + 3, *s_full = bars + 5,
+           *s_read = bars + 6, *p_full = bars + 7, *mma2_done = bars + 8, *hq_free = bars + 10,
+           *drain = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::oTmem);
+  volatile int* abort = reinterpret_cast<volatile int*>(smem + C::oAbort);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.y;
+  const int k0 = blockIdx.x * BK;
+  const int n_qt = (Tq + BQ - 1) / BQ;
+  const int i_begin = CAUSAL ? k0 / BQ : 0;
+  const int n_iter = n_qt > i_begin ? n_qt - i_begin : 0;
+
+  if (threadIdx.x == 0) {
+    tc::mbar_init(kv_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      tc::mbar_init(q_full + b, 1);
+      tc::mbar_init(q_empty + b, 1);
+      tc::mbar_init(mma2_done + b, 1);
+    }
+    tc::mbar_init(s_full, 1);
+    tc::mbar_init(s_read, NCOMPUTE);
+    tc::mbar_init(p_full, NCOMPUTE);
+    tc::mbar_init(hq_free, NDQ);
+    tc::mbar_init(drain, 1);
+    *abort = 0;
+    tc::fence_barrier_init();
+  }
+  if (warp == 1) tc::tmem_alloc(tmem_slot, 512);
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t t_hv = tmem + 256, t_hk = tmem + 256 + HD, t_hqp = tmem + 384;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0 && n_iter > 0) {
+      tc::mbar_expect_tx(kv_full, 4 * C::kKV);
+      for (int cb = 0; cb < HD / 64; ++cb) {
+        const int o = cb * BK * 128;
+        tc::tma_load_3d(smem + C::oK + o, &tm_k, kv_full, cb * 64, k0, bh);
+        tc::tma_load_3d(smem + C::oV + o, &tm_v, kv_full, cb * 64, k0, bh);
+        tc::tma_load_3d(smem + C::oTK + o, &tm_tk, kv_full, cb * 64, k0, bh);
+        tc::tma_load_3d(smem + C::oTV + o, &tm_tv, kv_full, cb * 64, k0, bh);
+      }
+      int issued = 0;
+      for (int t = 0; t < n_iter; ++t) {
+        const int st = t % ST;
+        if (t >= ST && !tc::mbar_wait(q_empty + st, ((t / ST) - 1) & 1, abort)) break;
+        const int q0 = (i_begin + t) * BQ;
+        uint8_t* base = smem + C::oQ + st * 3 * C::kQ;
+        tc::mbar_expect_tx(q_full + st, 3 * C::kQ);
+        for (int cb = 0; cb < HD / 64; ++cb) {
+          const int o = cb * BQ * 128;
+          tc::tma_load_3d(base + o, &tm_q, q_full + st, cb * 64, q0, bh);
+          tc::tma_load_3d(base + C::kQ + o, &tm_tq, q_full + st, cb * 64, q0, bh);
+          tc::tma_load_3d(base + 2 * C::kQ + o, &tm_w, q_full + st, cb * 64, q0, bh);
+        }
+        issued = t + 1;
+      }
+      tc::mbar_wait_drain(kv_full, 0);
+      for (int t = issued > ST ? issued - ST : 0; t < issued; ++t)
+        tc::mbar_wait_drain(q_full + t % ST, (t / ST) & 1);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0 && n_iter > 0) {
+      constexpr int ab = tc::AbFmt<T>::v;
+      constexpr uint32_t id_s = tc::idesc_f16(BK, BQ, ab, 0, 0);
+      constexpr uint32_t id_kv = tc::idesc_f16(BK, HD, ab, 0, 1);
+      constexpr uint32_t id_hqt = tc::idesc_f16(HD, BQ, ab, 1, 1);      // HD == 128
+      constexpr uint32_t id_hqp = tc::idesc_f16(2 * BQ, HD, ab, 1, 1);  // HD == 64
+      const uint32_t a_k = tc::smem_u32(smem + C::oK), a_v = tc::smem_u32(smem + C::oV);
+      const uint32_t a_tk = tc::smem_u32(smem + C::oTK), a_tv = tc::smem_u32(smem + C::oTV);
+      const uint32_t a_pd = tc::smem_u32(smem + C::oPd);
+      const uint32_t a_ds = tc::smem_u32(smem + C::oDS), a_dsd = tc::smem_u32(smem + C::oDSd);
+      bool ok = tc::mbar_wait(kv_full, 0, abort);
+      for (int t = 0; ok && t < n_iter; ++t) {
+        const int st = t % ST;
+        const int b = kPair ? (t & 1) : 0;
+        const uint32_t a_q = tc::smem_u32(smem + C::oQ + st * 3 * C::kQ);
+        const uint32_t a_tq = a_q + C::kQ, a_w = a_q + 2 * C::kQ;
+        if (!tc::mbar_wait(q_full + st, (t / ST) & 1, abort)) break;
+        if (t >= 1 && !tc::mbar_wait(s_read, (t - 1) & 1, abort)) break;
+        if (!kPair && t >= 1 && !tc::mbar_wait(hq_free, (t - 1) & 1, abort)) break;
+        tc::tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t oa = (kk / 4) * (BK * 128) + (kk % 4) * 32;
+          const uint32_t ob = (kk / 4) * (BQ * 128) + (kk % 4) * 32;
+          const uint32_t acc = kk > 0 ? 1u : 0u;
+          auto d = [](uint32_t a) { return tc::sw128_desc(a, 16, 1024); };
+          tc::mma_ss(tmem + 0, d(a_k + oa), d(a_q + ob), id_s, acc);      // S^T
+          tc::mma_ss(tmem + 64, d(a_k + oa), d(a_tq + ob), id_s, acc);    // Sd'^T
+          tc::mma_ss(tmem + 64, d(a_tk + oa), d(a_q + ob), id_s, 1u);
+          tc::mma_ss(tmem + 128, d(a_v + oa), d(a_w + ob), id_s, acc);    // dP^T
+          tc::mma_ss(tmem + 192, d(a_tv + oa), d(a_w + ob), id_s, acc);   // dPd^T
+        }
+        tc::mma_commit(s_full);
+        if (!tc::mbar_wait(p_full, t & 1, abort)) break;
+        tc::tc_fence_after();
+        const uint32_t ds_b = a_ds + b * C::kP, dsd_b = a_dsd + b * C::kP;
+#pragma unroll
+        for (int kk = 0; kk < BQ / 16; ++kk) {
+          const uint32_t ob = kk * 16 * 128;
+          const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
+          auto dk_ = [](uint32_t a) { return tc::sw128_desc(a, 16, 1024); };
+          auto dm = [](uint32_t a) { return tc::sw128_desc(a, BQ * 128, 1024); };
+          tc::mma_ss(t_hk, dk_(dsd_b + kk * 32), dm(a_q + ob), id_kv, acc);   // dSd^T Q
+          tc::mma_ss(t_hk, dk_(ds_b + kk * 32), dm(a_tq + ob), id_kv, 1u);    // dS^T tQ
+          tc::mma_ss(t_hv, dk_(a_pd + kk * 32), dm(a_w + ob), id_kv, acc);    // Pd^T W
+        }
+        if constexpr (!kPair) {
+          // hQ^T = K^T dSd^T + tK^T dS^T, into the S^T columns
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint32_t o = kk * 2048;
+            tc::mma_ss(tmem, tc::sw128_desc(a_k + o, BK * 128, 1024),
+                       tc::sw128_desc(dsd_b + o, BK * 128, 1024), id_hqt, kk > 0 ? 1u : 0u);
+            tc::mma_ss(tmem, tc::sw128_desc(a_tk + o, BK * 128, 1024),
+                       tc::sw128_desc(ds_b + o, BK * 128, 1024), id_hqt, 1u);
+          }
+        } else if ((t & 1) || t == n_iter - 1) {
+          // hQ = dSd K + dS tK for the pair (2p, 2p+1)
+          const int p = t >> 1;
+          if (p > 0 && !tc::mbar_wait(hq_free, (p - 1) & 1, abort)) break;
+          tc::tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint32_t o = kk * 2048;
+            tc::mma_ss(t_hqp, tc::sw128_desc(a_dsd + o, C::kP, 1024),
+                       tc::sw128_desc(a_k + o, BK * 128, 1024), id_hqp, kk > 0 ? 1u : 0u);
+            tc::mma_ss(t_hqp, tc::sw128_desc(a_ds + o, C::kP, 1024),
+                       tc::sw128_desc(a_tk + o, BK * 128, 1024), id_hqp, 1u);
+          }
+        }
+        tc::mma_commit(mma2_done + (t & 1));
+        tc::mma_commit(q_empty + st);
+      }
+      tc::mma_commit(drain);
+      tc::mbar_wait_drain(drain, 0);
+    }
+  } else if (warp < 2 + NCOMPUTE / 32) {
+    // ------------------------------------------------------------ compute
+    const int grp = (warp - 2) >> 2;
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;  // TMEM lane = key row
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const int key = k0 + r;
+    bool ok = true;
+    auto wait = [&](uint64_t* bar, uint32_t parity) {
+      return __all_sync(0xffffffffu, tc::mbar_wait(bar, parity, abort));
+    };
+    const uint32_t a_pd = tc::smem_u32(smem + C::oPd);
+    const uint32_t a_ds = tc::smem_u32(smem + C::oDS), a_dsd = tc::smem_u32(smem + C::oDSd);
+    const size_t row_base = (size_t)bh * Tq;
+    for (int t = 0; t < n_iter; ++t) {
+      const int b = kPair ? (t & 1) : 0;
+      const int q0 = (i_begin + t) * BQ;
+      const int ql = q0 + grp * 32 + lane;
+      const bool qin = ql < Tq;
+      const float my_l = qin ? __ldg(lse + row_base + ql) * 1.4426950408889634f : INFINITY;
+      const float my_c = qin ? __ldg(stats + row_base + ql) : 0.f;
+      const float my_z = qin ? __ldg(stats + n_rows_total + row_base + ql) : 0.f;
+      const float my_zd = qin ? __ldg(stats + 2 * n_rows_total + row_base + ql) : 0.f;
+      if (!wait(s_full, t & 1)) { ok = false; break; }
+      tc::tc_fence_after();
+      float sv[32], sd[32], dp[32], dpd[32];
+      const uint32_t c0 = tmem + lane_off + grp * 32;
+      tc::tmem_ld32(c0, sv);
+      tc::tmem_ld32(c0 + 64, sd);
+      tc::tmem_ld32(c0 + 128, dp);
+      tc::tmem_ld32(c0 + 192, dpd);
+      tc::tc_fence_before();
+      tc::mbar_arrive(s_read);
+      const bool diag = CAUSAL && (q0 < k0 + BK);
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        const float lq = __shfl_sync(0xffffffffu, my_l, e);
+        const float cq = __shfl_sync(0xffffffffu, my_c, e);
+        const float zq = __shfl_sync(0xffffffffu, my_z, e);
+        const float zdq = __shfl_sync(0xffffffffu, my_zd, e);
+        float p = tc::ex2(sv[e] * scale_log2 - lq);
+        if (key >= M || (diag && q0 + grp * 32 + e < key)) p = 0.f;
+        const float pd = p * (sd[e] * scale - cq);
+        const float g = dp[e] - zq;
+        sv[e] = pd;                                  // Pd^T
+        sd[e] = p * g;                               // dS^T
+        dp[e] = pd * g + p * (dpd[e] - zdq);         // dSd^T
+      }
+      // every tile written below was last read by tile t-1's MMAs
+      if (t >= 1 && !wait(mma2_done + ((t - 1) & 1), ((t - 1) >> 1) & 1)) { ok = false; break; }
+      const uint32_t bpd = a_pd, bds = a_ds + b * C::kP, bdsd = a_dsd + b * C::kP;
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const uint32_t off = tc::sw128_off(r, grp * 4 + h);
+        const float* x = sv + h * 8;
+        const float* y = sd + h * 8;
+        const float* zz = dp + h * 8;
+        tc::st_shared_v4(bpd + off, tc::pack2<T>(x[0], x[1]), tc::pack2<T>(x[2], x[3]),
+                         tc::pack2<T>(x[4], x[5]), tc::pack2<T>(x[6], x[7]));
+        tc::st_shared_v4(bds + off, tc::pack2<T>(y[0], y[1]), tc::pack2<T>(y[2], y[3]),
+                         tc::pack2<T>(y[4], y[5]), tc::pack2<T>(y[6], y[7]));
+        tc::st_shared_v4(bdsd + off, tc::pack2<T>(zz[0], zz[1]), tc::pack2<T>(zz[2], zz[3]),
+                         tc::pack2<T>(zz[4], zz[5]), tc::pack2<T>(zz[6], zz[7]));
+      }
+      tc::fence_proxy_async_smem();
+      tc::tc_fence_before();
+      tc::mbar_arrive(p_full);
+    }
+    // ------------------------------------------------------------ hK, hV
+    if (ok && n_iter > 0) {
+      const int tl = n_iter - 1;
+      ok = wait(mma2_done + (tl & 1), (tl >> 1) & 1);
+      if (ok) tc::tc_fence_after();
+    }
+    if (ok) {
+      const bool store = key < M;
+      const size_t base = ((size_t)bh * M + (store ? key : 0)) * HD;
+#pragma unroll 1
+      for (int which = 0; which < 2; ++which) {
+        T* out = which == 0 ? hv : hk;
+        if (out == nullptr) continue;
+        const float mul = which == 0 ? 1.f : scale;
+        const uint32_t col = which == 0 ? t_hv : t_hk;
+#pragma unroll 1
+        for (int c = grp * (HD / 64); c < (grp + 1) * (HD / 64); ++c) {
+          float v[32];
+          if (n_iter > 0) {
+            tc::tmem_ld32(col + lane_off + c * 32, v);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = 0.f;
+          }
+          if (!store) continue;
+          uint4* d4 = reinterpret_cast<uint4*>(out + base + c * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float* e = v + 8 * i;
+            d4[i] = make_uint4(tc::pack2<T>(e[0] * mul, e[1] * mul),
+                               tc::pack2<T>(e[2] * mul, e[3] * mul),
+                               tc::pack2<T>(e[4] * mul, e[5] * mul),
+                               tc::pack2<T>(e[6] * mul, e[7] * mul));
+          }
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ hQ flush
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const size_t row_base = (size_t)bh * Tq;
+    auto wait = [&](uint64_t* bar, uint32_t parity) {
+      return __all_sync(0xffffffffu, tc::mbar_wait(bar, parity, abort));
+    };
+    for (int t = 0; t < n_iter; ++t) {
+      if (kPair && !(t & 1) && t != n_iter - 1) continue;
+      if (!wait(mma2_done + (t & 1), (t >> 1) & 1)) break;
+      tc::tc_fence_after();
+      if constexpr (!kPair) {
+        const int qb = (i_begin + t) * BQ;
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          float v[32];
+          tc::tmem_ld32(tmem + lane_off + c * 32, v);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int q = qb + c * 32 + e;
+            if (q < Tq) atomicAdd(hq_acc + (row_base + q) * HD + r, v[e] * scale);
+          }
+        }
+      } else {
+        const int q = (i_begin + (t & ~1)) * BQ + r;
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          float v[32];
+          tc::tmem_ld32(t_hqp + lane_off + c * 32, v);
+          if (q < Tq) {
+            float* dst = hq_acc + (row_base + q) * HD + c * 32;
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              tcbwd::red_add_v4(dst + 4 * i, v[4 * i] * scale, v[4 * i + 1] * scale,
+                                v[4 * i + 2] * scale, v[4 * i + 3] * scale);
+          }
+        }
+      }
+      tc::tc_fence_before();
+      tc::mbar_arrive(hq_free);
+    }
+  }
+  // ------------------------------------------------------------ teardown
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace tchvp
+}  // namespace theria

@@ -217,7 +217,9 @@ jvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
         const int col = col0 + e;
         const bool valid = col < M && (!CAUSAL || col <= row);
         const float p = valid ? tc::ex2(sv[e] * scale_log2 - lse2) : 0.f;
-        const float u = p * (sd[e] * scale);
+        // c is summed from U as rounded for the MMA, so that OA - c OP
+        // cancels consistently (a row with one key gives Odot = tV exactly).
+        const float u = to_f32<T>(from_f32<T>(p * (sd[e] * scale)));
         c_acc += u;
         sv[e] = p;
         sd[e] = u;

@@ -14,6 +14,7 @@
 #include "sdpa_tc_bwd.cuh"
 #include "sdpa_tc_fwd.cuh"
 #include "sdpa_tc_jvp.cuh"
+#include "sdpa_tc_hvp.cuh"
 #include "tc_host.cuh"
 
 namespace theria {
@@ -292,6 +293,59 @@ int tc_jvp(const void* q, const void* k, const void* v, const void* tq, const vo
 #undef THERIA_JVP
 }
 
+int64_t simt_hvp_ws(const Shape& s) { return align_up(3 * s.B * s.H * s.T * 4); }
+int64_t tc_hvp_ws(const Shape& s) {
+  return align_up(3 * s.B * s.H * s.T * 4) + align_up(s.B * s.H * s.T * s.D * 4);
+}
+
+template <typename T, int HD, bool CAUSAL>
+int tc_hvp_launch(const CUtensorMap* m, const float* lse, const float* stats, float* hq_acc,
+                  void* hk, void* hv, const Shape& s, cudaStream_t st) {
+  using C = tchvp::Cfg<HD>;
+  auto kern = tchvp::hvp_kernel<T, HD, CAUSAL>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kAlloc);
+  dim3 grid((unsigned)((s.M + tchvp::BK - 1) / tchvp::BK), (unsigned)(s.B * s.H));
+  kern<<<grid, tchvp::NTHREADS, C::kAlloc, st>>>(m[0], m[1], m[2], m[3], m[4], m[5], m[6], lse,
+                                                 stats, s.B * s.H * s.T, hq_acc, (T*)hk,
+                                                 (T*)hv, (int)s.T, (int)s.M, s.scale,
+                                                 s.scale * 1.4426950408889634f);
+  return launch_status();
+}
+
+// Tensor-core HVP: pass 1 (JVP kernel with W) then the fused hQ/hK/hV pass;
+// -1 when no TMA descriptor fits.
+template <typename T>
+int tc_hvp(const void* q, const void* k, const void* v, const void* w, const float* lse,
+           const void* tq, const void* tk, const void* tv, void* hq, void* hk, void* hv,
+           void* o_tan, void* ws, const Shape& s, int dtype, cudaStream_t st) {
+  CUtensorMap m[7];
+  const int64_t bh = s.B * s.H;
+  const void* src[7] = {q, tq, w, k, v, tk, tv};
+  for (int i = 0; i < 7; ++i)
+    if (!tc::make_map_3d(&m[i], src[i], dtype, bh, i < 3 ? s.T : s.M, s.D,
+                         i < 3 ? (uint32_t)tchvp::BQ : (uint32_t)tchvp::BK))
+      return -1;
+  float* stats = (float*)ws;
+  float* hq_acc = (float*)((char*)ws + align_up(3 * bh * s.T * 4));
+  int e = tc_jvp<T>(q, k, v, tq, tk, tv, w, lse, o_tan, stats, s, dtype, st);
+  if (e != 0) return e;
+  const int64_t n = bh * s.T * s.D;
+  if (cudaMemsetAsync(hq_acc, 0, n * 4, st) != cudaSuccess) return THERIA_ERR_LAUNCH;
+  if (s.D == 64)
+    e = s.causal ? tc_hvp_launch<T, 64, true>(m, lse, stats, hq_acc, hk, hv, s, st)
+                 : tc_hvp_launch<T, 64, false>(m, lse, stats, hq_acc, hk, hv, s, st);
+  else
+    e = s.causal ? tc_hvp_launch<T, 128, true>(m, lse, stats, hq_acc, hk, hv, s, st)
+                 : tc_hvp_launch<T, 128, false>(m, lse, stats, hq_acc, hk, hv, s, st);
+  if (e) return e;
+  if (hq != nullptr) {
+    const unsigned blocks = (unsigned)std::min<int64_t>((n / 4 + 255) / 256, 148 * 16);
+    tcbwd::finish_kernel<T><<<blocks, 256, 0, st>>>(hq_acc, (T*)hq, n);
+    return launch_status();
+  }
+  return THERIA_OK;
+}
+
 bool use_tc(int dtype, const Shape& s, std::initializer_list<const void*> ptrs) {
   if (!tc::tc_eligible(dtype, s.T, s.M, s.D, s.B * s.H)) return false;
   for (const void* p : ptrs)
@@ -357,9 +411,10 @@ int64_t theria_sdpa_bwd_workspace_bytes(int64_t B, int64_t H, int64_t T, int64_t
 
 int64_t theria_sdpa_hvp_workspace_bytes(int64_t B, int64_t H, int64_t T, int64_t M,
                                         int64_t D) {
-  (void)M;
-  (void)D;
-  return align_up(3 * B * H * T * (int64_t)sizeof(float));
+  Shape s{B, H, T, M, D, 1.f, 0};
+  // Row terms (c, z, zdot), plus the fp32 hQ accumulator of the tensor-core
+  // path where the head dim allows it.
+  return (D == 64 || D == 128) ? tc_hvp_ws(s) : simt_hvp_ws(s);
 }
 
 int theria_sdpa_bwd(const void* q, const void* k, const void* v, const void* o, int o_dtype,
@@ -415,10 +470,18 @@ int theria_sdpa_hvp(const void* q, const void* k, const void* v, const void* w,
   if (int e = check_shape(B, H, T, M, D, dtype)) return e;
   if (empty_problem(B, H, T)) return THERIA_OK;
   if (!q || !k || !v || !w || !lse || !tq || !tk || !tv) return THERIA_ERR_INVALID_ARG;
-  if (!workspace || workspace_bytes < theria_sdpa_hvp_workspace_bytes(B, H, T, M, D))
-    return THERIA_ERR_WORKSPACE;
   Shape s{B, H, T, M, D, scale, causal ? 1 : 0};
+  if (!workspace || workspace_bytes < simt_hvp_ws(s)) return THERIA_ERR_WORKSPACE;
   cudaStream_t st = (cudaStream_t)stream;
+  if (workspace_bytes >= tc_hvp_ws(s) &&
+      use_tc(dtype, s, {q, k, v, w, tq, tk, tv, hq, hk, hv, o_tan})) {
+    int e = dtype == THERIA_BF16
+                ? tc_hvp<__nv_bfloat16>(q, k, v, w, lse, tq, tk, tv, hq, hk, hv, o_tan,
+                                        workspace, s, dtype, st)
+                : tc_hvp<__half>(q, k, v, w, lse, tq, tk, tv, hq, hk, hv, o_tan, workspace, s,
+                                 dtype, st);
+    if (e >= 0) return e;
+  }
   return THERIA_DISPATCH(dtype, simt_hvp, q, k, v, w, lse, tq, tk, tv, hq, hk, hv, o_tan,
                          (float*)workspace, s, st);
 }
