@@ -33,11 +33,18 @@ def _draw(shape_q, shape_k, dtype, seed=0, n_q=4, n_k=5):
     return qs, ks
 
 
-def _check(x, ref, dtype, hvp=False):
+def _check(x, ref, dtype, hvp=False, causal=False):
     if dtype == torch.float32:
         tol = TOL_REL_HVP if hvp else TOL_REL
         err = max_rel(x, ref)
         assert err <= tol, f"max rel err {err:.3e} > {tol}"
+    elif hvp and causal:
+        # Causal rows with few keys give second-order values of several
+        # units, where 16-bit operands and a 16-bit output alone carry
+        # ~1% error: use the reference's own 16-bit criterion
+        # (torch.testing.assert_close(rtol=2e-2, atol=2e-2),
+        # tests/test_triton_fused_forward.py:31 in theria).
+        torch.testing.assert_close(x.detach().float().cpu(), ref.float(), rtol=2e-2, atol=2e-2)
     else:
         err = max_abs(x, ref)
         assert err <= TOL_ABS_LP, f"max abs err {err:.3e} > {TOL_ABS_LP}"
@@ -116,7 +123,7 @@ def test_jvp_and_hvp_match_oracle(shape, dtype, causal):
                               causal=causal)
     ref = orc.hvp(*f, causal=causal)
     for x, r in zip((hq, hk, hv, ot2), ref):
-        _check(x, r, dtype, hvp=True)
+        _check(x, r, dtype, hvp=True, causal=causal)
 
 
 def test_outputs_can_be_skipped():
