@@ -418,6 +418,29 @@ def theria_arm(args, world, rank, local):
     print(json.dumps(line), flush=True)
 
 
+def profile_case(case):
+    """A few launches of one operator at a size ncu can capture in minutes
+    (inputs still larger than L2): --profile-case fwdbwd|jvp|hvp."""
+    from theria_b200.attention import ops
+    torch.cuda.set_device(0)
+    if case == "fwdbwd":
+        shape = (1, 16, 4096, 128)
+    else:
+        shape = (CFG3["B"], CFG3["H"], CFG3["N"], CFG3["D"])
+    gen = torch.Generator("cpu").manual_seed(0)
+    q, k, v, w, tq, tk, tv = (randn(shape, gen, torch.bfloat16, "cuda") for _ in range(7))
+    for _ in range(3):
+        o, lse = ops.forward(q, k, v)
+        if case == "fwdbwd":
+            ops.backward(q, k, v, w, lse, o=o)
+        elif case == "jvp":
+            ops.jvp(q, k, v, tq, tk, tv, lse)
+        else:
+            ops.hvp(q, k, v, w, lse, tq, tk, tv)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_case": case, "shape": list(shape), "ok": True}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -428,7 +451,12 @@ def main():
     ap.add_argument("--no-extra", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=12.0,
                     help="seconds of CPU work for the cpu_baseline sample")
+    ap.add_argument("--profile-case", choices=["fwdbwd", "jvp", "hvp"], default=None,
+                    help="run a few launches of one operator for ncu, print no bench line")
     args = ap.parse_args()
+    if args.profile_case:
+        profile_case(args.profile_case)
+        return
     if args.warmup < 3:
         args.warmup = 3  # timing rule: at least 3 warm-up steps
     world, rank, local = (int(os.environ.get("WORLD_SIZE", "1")),
