@@ -47,3 +47,25 @@ def test_full_vs_first_order_differ_and_sequential_matches_batched():
     g_fo = _grad(m, fo)
     assert ((g_bat - g_fo).norm() / g_bat.norm()).item() > 1e-3
     assert torch.isfinite(g_bat).all()
+
+
+def test_graphed_meta_step_matches_eager():
+    from theria_b200.maml.distributed import GraphedMetaStep, MetaStep
+    torch.manual_seed(2)
+    m1 = MAMLClassifier(ModelConfig()).cuda()
+    m2 = MAMLClassifier(ModelConfig()).cuda()
+    m2.load_state_dict(m1.state_dict())
+    batches = [stack_tasks(sample_tasks(40 + i, 4)).to("cuda") for i in range(3)]
+    eager = MetaStep(m1, meta_batch=4, inner_steps=2, capturable=True)
+    graphed_ms = MetaStep(m2, meta_batch=4, inner_steps=2, capturable=True)
+    # capture warms up on the first batch (3 steps); mirror that in eager
+    g = GraphedMetaStep(graphed_ms, batches[0], warmup=3)
+    for _ in range(3):
+        eager.step(batches[0])
+    for b in batches:
+        l1 = eager.step(b)
+        l2 = g.step(b)
+    torch.cuda.synchronize()
+    assert abs(l1.item() - l2.item()) <= 1e-4 * abs(l1.item())
+    for p1, p2 in zip(m1.parameters(), m2.parameters()):
+        assert (p1 - p2).abs().max().item() <= 1e-4 * max(1.0, p1.abs().max().item())

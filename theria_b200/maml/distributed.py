@@ -41,7 +41,7 @@ class MetaStep:
     """One outer step: local batched adaptation, one gradient all-reduce, Adam."""
 
     def __init__(self, model, *, meta_batch=32, inner_lr=0.4, inner_steps=5, fo=False,
-                 outer_lr=1e-3, world=1):
+                 outer_lr=1e-3, world=1, capturable=False):
         self.model = model
         self.meta_batch = meta_batch
         self.inner_lr = inner_lr
@@ -49,7 +49,7 @@ class MetaStep:
         self.fo = fo
         self.world = world
         self.params = [p for p in model.parameters()]
-        self.opt = torch.optim.Adam(self.params, lr=outer_lr)
+        self.opt = torch.optim.Adam(self.params, lr=outer_lr, capturable=capturable)
         n = sum(p.numel() for p in self.params)
         self.bucket = torch.zeros(n, dtype=torch.float32, device=self.params[0].device)
 
@@ -71,11 +71,12 @@ class MetaStep:
             dist.all_reduce(self.bucket, op=dist.ReduceOp.SUM)
 
     def apply(self) -> None:
-        off = 0
-        for p in self.params:
-            n = p.numel()
-            p.grad = self.bucket[off:off + n].view_as(p)
-            off += n
+        if self.params[0].grad is None:
+            off = 0
+            for p in self.params:
+                n = p.numel()
+                p.grad = self.bucket[off:off + n].view_as(p)  # views of the bucket
+                off += n
         self.opt.step()
 
     def step(self, tasks: TaskBatch) -> torch.Tensor:
@@ -83,3 +84,42 @@ class MetaStep:
         self.exchange()
         self.apply()
         return loss
+
+
+class GraphedMetaStep:
+    """A MetaStep captured once into a CUDA graph and replayed every step.
+
+    The meta-step is hundreds of small kernels (two encoder layers, five
+    inner SGD steps with create_graph=True, the query loss, the
+    second-order backward, the gradient all-reduce and Adam); at this
+    model size launching them costs more than running them.  Capture
+    records the whole step once; each call then copies the new task batch
+    into the captured input buffers and replays the graph.
+
+    The wrapped MetaStep's optimizer must be built with capturable=True
+    (``MetaStep(..., capturable=True)``); the task batch shapes are fixed
+    at capture.  Under torch.distributed the all-reduce is captured too
+    (NCCL supports capture; the communicator is warmed up first).
+    """
+
+    def __init__(self, meta_step: "MetaStep", example: TaskBatch, warmup: int = 3):
+        self.ms = meta_step
+        dev = meta_step.bucket.device
+        self.static = TaskBatch(*(t.to(dev).clone() for t in
+                                  (example.x_s, example.y_s, example.x_q, example.y_q)))
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                self.ms.step(self.static)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.loss = self.ms.step(self.static)
+
+    def step(self, tasks: TaskBatch) -> torch.Tensor:
+        for dst, src in zip((self.static.x_s, self.static.y_s, self.static.x_q, self.static.y_q),
+                            (tasks.x_s, tasks.y_s, tasks.x_q, tasks.y_q)):
+            dst.copy_(src, non_blocking=True)
+        self.graph.replay()
+        return self.loss
