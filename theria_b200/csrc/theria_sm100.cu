@@ -11,6 +11,7 @@
 
 #include "common.cuh"
 #include "sdpa_simt.cuh"
+#include "sdpa_small.cuh"
 #include "sdpa_tc_bwd.cuh"
 #include "sdpa_tc_fwd.cuh"
 #include "sdpa_tc_jvp.cuh"
@@ -156,6 +157,72 @@ int simt_hvp(const void* q, const void* k, const void* v, const void* w, const f
     if (int e = launch_status()) return e;
   }
   return THERIA_OK;
+}
+
+// ------------------------------------------------------ whole-head launches
+bool small_eligible(const Shape& s) {
+  return s.T <= small::MAXN && s.M <= small::MAXN && s.D <= small::MAXD && s.B * s.H < (1ll << 31);
+}
+
+template <typename K>
+void small_setup(K kern, size_t bytes) {
+  if (bytes > 48 * 1024)
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+}
+
+template <typename T>
+int small_fwd(const void* q, const void* k, const void* v, void* o, int o_dtype, float* lse,
+              const Shape& s, cudaStream_t st) {
+  const size_t sm = small::smem_bytes((int)s.T, (int)s.M, (int)s.D, 1, 2, 1);
+  const unsigned grid = (unsigned)(s.B * s.H);
+  if (o_dtype == THERIA_F32) {
+    auto kern = small::fwd_kernel<T, float>;
+    small_setup(kern, sm);
+    kern<<<grid, small::NTHREADS, sm, st>>>((const T*)q, (const T*)k, (const T*)v, (float*)o,
+                                            lse, s);
+  } else {
+    auto kern = small::fwd_kernel<T, T>;
+    small_setup(kern, sm);
+    kern<<<grid, small::NTHREADS, sm, st>>>((const T*)q, (const T*)k, (const T*)v, (T*)o, lse,
+                                            s);
+  }
+  return launch_status();
+}
+
+template <typename T>
+int small_bwd(const void* q, const void* k, const void* v, const void* dout, const float* lse,
+              void* dq, void* dk, void* dv, const Shape& s, cudaStream_t st) {
+  const size_t sm = small::smem_bytes((int)s.T, (int)s.M, (int)s.D, 2, 2, 2);
+  auto kern = small::bwd_kernel<T>;
+  small_setup(kern, sm);
+  kern<<<(unsigned)(s.B * s.H), small::NTHREADS, sm, st>>>(
+      (const T*)q, (const T*)k, (const T*)v, (const T*)dout, lse, (T*)dq, (T*)dk, (T*)dv, s);
+  return launch_status();
+}
+
+template <typename T>
+int small_jvp(const void* q, const void* k, const void* v, const void* tq, const void* tk,
+              const void* tv, const float* lse, void* o_tan, const Shape& s, cudaStream_t st) {
+  const size_t sm = small::smem_bytes((int)s.T, (int)s.M, (int)s.D, 2, 4, 2);
+  auto kern = small::jvp_kernel<T>;
+  small_setup(kern, sm);
+  kern<<<(unsigned)(s.B * s.H), small::NTHREADS, sm, st>>>(
+      (const T*)q, (const T*)k, (const T*)v, (const T*)tq, (const T*)tk, (const T*)tv, lse,
+      (T*)o_tan, s);
+  return launch_status();
+}
+
+template <typename T>
+int small_hvp(const void* q, const void* k, const void* v, const void* w, const float* lse,
+              const void* tq, const void* tk, const void* tv, void* hq, void* hk, void* hv,
+              void* o_tan, const Shape& s, cudaStream_t st) {
+  const size_t sm = small::smem_bytes((int)s.T, (int)s.M, (int)s.D, 3, 4, 4);
+  auto kern = small::hvp_kernel<T>;
+  small_setup(kern, sm);
+  kern<<<(unsigned)(s.B * s.H), small::NTHREADS, sm, st>>>(
+      (const T*)q, (const T*)k, (const T*)v, (const T*)w, lse, (const T*)tq, (const T*)tk,
+      (const T*)tv, (T*)hq, (T*)hk, (T*)hv, (T*)o_tan, s);
+  return launch_status();
 }
 
 // ------------------------------------------------------ tensor-core launches
@@ -393,6 +460,7 @@ int theria_sdpa_fwd(const void* q, const void* k, const void* v, void* o, int o_
   if (!q || !k || !v || !o) return THERIA_ERR_INVALID_ARG;
   Shape s{B, H, T, M, D, scale, causal ? 1 : 0};
   cudaStream_t st = (cudaStream_t)stream;
+  if (small_eligible(s)) return THERIA_DISPATCH(dtype, small_fwd, q, k, v, o, o_dtype, lse, s, st);
   if (use_tc(dtype, s, {q, k, v, o})) {
     int e = dtype == THERIA_BF16 ? tc_fwd<__nv_bfloat16>(q, k, v, o, o_dtype, lse, s, dtype, st)
                                  : tc_fwd<__half>(q, k, v, o, o_dtype, lse, s, dtype, st);
@@ -428,6 +496,8 @@ int theria_sdpa_bwd(const void* q, const void* k, const void* v, const void* o, 
   Shape s{B, H, T, M, D, scale, causal ? 1 : 0};
   if (!workspace || workspace_bytes < simt_bwd_ws(s)) return THERIA_ERR_WORKSPACE;
   cudaStream_t st = (cudaStream_t)stream;
+  if (small_eligible(s))
+    return THERIA_DISPATCH(dtype, small_bwd, q, k, v, dout, lse, dq, dk, dv, s, st);
   // The tensor-core path needs the larger workspace; a caller that passes
   // only the minimum (row terms) gets the CUDA-core kernels.
   if (workspace_bytes >= tc_bwd_ws(s) && use_tc(dtype, s, {q, k, v, o, dout, dq, dk, dv})) {
@@ -451,6 +521,8 @@ int theria_sdpa_jvp(const void* q, const void* k, const void* v, const void* tq,
   if (!q || !k || !v || !tq || !tk || !tv || !lse || !o_tan) return THERIA_ERR_INVALID_ARG;
   Shape s{B, H, T, M, D, scale, causal ? 1 : 0};
   cudaStream_t st = (cudaStream_t)stream;
+  if (small_eligible(s))
+    return THERIA_DISPATCH(dtype, small_jvp, q, k, v, tq, tk, tv, lse, o_tan, s, st);
   if (use_tc(dtype, s, {q, k, v, tq, tk, tv, o_tan})) {
     int e = dtype == THERIA_BF16
                 ? tc_jvp<__nv_bfloat16>(q, k, v, tq, tk, tv, nullptr, lse, o_tan, nullptr, s,
@@ -473,6 +545,9 @@ int theria_sdpa_hvp(const void* q, const void* k, const void* v, const void* w,
   Shape s{B, H, T, M, D, scale, causal ? 1 : 0};
   if (!workspace || workspace_bytes < simt_hvp_ws(s)) return THERIA_ERR_WORKSPACE;
   cudaStream_t st = (cudaStream_t)stream;
+  if (small_eligible(s))
+    return THERIA_DISPATCH(dtype, small_hvp, q, k, v, w, lse, tq, tk, tv, hq, hk, hv, o_tan, s,
+                           st);
   if (workspace_bytes >= tc_hvp_ws(s) &&
       use_tc(dtype, s, {q, k, v, w, tq, tk, tv, hq, hk, hv, o_tan})) {
     int e = dtype == THERIA_BF16
