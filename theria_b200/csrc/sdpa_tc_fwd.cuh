@@ -1,21 +1,24 @@
 // Tensor-core (tcgen05) SDPA forward for bf16/fp16 with head dim 64 or 128.
 //
-// One CTA owns a 128-row query tile of one (batch, head) and streams the
-// keys in tiles of 128.  Warp roles:
-//   warp 0      TMA producer: Q once, then K and V tiles into a 2-stage ring
-//   warp 1      MMA issuer (one thread) and TMEM owner
-//   warps 2..5  softmax + epilogue, one query row per thread (TMEM lane)
-// TMEM (512 columns): S double buffer at columns [0,128) and [128,256),
-// the O accumulator at [256, 256+HD).
-// Per key tile j the MMA thread issues S_{j+1} = Q K_{j+1}^T before waiting
-// for P_j, so the QK^T of the next tile overlaps this tile's softmax, then
-// O += P_j V_j with P_j (16-bit, written by the softmax warps into a
-// double-buffered SW128 shared tile) as the A operand and V as an MN-major
-// B operand.
-// Softmax runs in the log2 domain with a lazily updated row maximum: O and
-// l are rescaled only when the running maximum grows by more than 8 (P stays
-// <= 2^8, fp32 cannot overflow); the final O / l is exact either way.  The
-// epilogue writes O (input dtype or fp32) and LSE = ln(2) * (m + log2 l).
+// One CTA owns TWO 128-row query tiles of one (batch, head) and streams the
+// keys in tiles of 128 through a 2-stage K/V ring.  Warp roles:
+//   warp 0       TMA producer: both Q tiles once, then K and V tiles
+//   warp 1       MMA issuer (one thread) and TMEM owner
+//   warps 4..7   softmax + epilogue of query tile 0 (one row per thread)
+//   warps 8..11  softmax + epilogue of query tile 1
+// TMEM (512 columns): S_t at [128t, 128t+128) and O_t at [256 + t*D, ...).
+// The tensor core alternates between the tiles (S_0, S_1, PV_0, PV_1, ...)
+// so that one tile's softmax runs while the other tile's MMAs do.
+// Softmax reads S in two passes (row max, then exponentials) so a thread
+// holds 32 scores at a time, and writes P as packed 16-bit pairs over the
+// first 64 columns of its own S; the PV MMA then takes P straight from TMEM
+// as its A operand (no shared-memory round trip).  In-order completion of
+// one thread's tcgen05 operations makes this safe: S_t(j+1) is issued after
+// PV_t(j), and the softmax waits for S_t(j+1) before touching S_t again,
+// which also guarantees PV_t(j) has finished with P and with O_t.
+// Softmax runs in the log2 domain with a lazily updated row maximum (O and
+// l rescaled only when the maximum grows by more than 8).  The epilogue
+// writes O (input dtype or fp32) and LSE = ln(2) * (m + log2 l).
 #pragma once
 
 #include "tc_common.cuh"
@@ -23,24 +26,23 @@
 namespace theria {
 namespace tcfwd {
 
-constexpr int BM = 128;      // query rows per CTA
+constexpr int BM = 128;      // rows per query tile
+constexpr int NQT = 2;       // query tiles per CTA
 constexpr int BN = 128;      // keys per tile
 constexpr int STAGES = 2;    // K/V ring depth
-constexpr int NTHREADS = 192;
+constexpr int NTHREADS = 384;
 constexpr float kRescaleThreshold = 8.f;  // log2 units
 
 template <int HD>
 struct Smem {
-  static constexpr int kQ = BM * HD * 2;
+  static constexpr int kQ = BM * HD * 2;  // one query tile
   static constexpr int kKV = BN * HD * 2;
-  static constexpr int kP = BM * BN * 2;
   static constexpr int oQ = 0;
-  static constexpr int oK = oQ + kQ;
+  static constexpr int oK = oQ + NQT * kQ;
   static constexpr int oV = oK + STAGES * kKV;
-  static constexpr int oP = oV + STAGES * kKV;
-  static constexpr int oBar = oP + 2 * kP;
-  // barriers: q_full, k_full[S], v_full[S], kv_empty[S], s_full[2],
-  // p_full[2], o_done[2], drain
+  static constexpr int oBar = oV + STAGES * kKV;
+  // q_full, k_full[S], v_full[S], kv_empty[S], s_full[2], p_full[2],
+  // o_done[2], drain
   static constexpr int nBar = 1 + 3 * STAGES + 6 + 1;
   static constexpr int oTmem = oBar + nBar * 8;
   static constexpr int oAbort = oTmem + 4;
@@ -62,19 +64,19 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
   uint64_t* k_full = bars + 1;
   uint64_t* v_full = k_full + STAGES;
   uint64_t* kv_empty = v_full + STAGES;
-  uint64_t* s_full = kv_empty + STAGES;
-  uint64_t* p_full = s_full + 2;
-  uint64_t* o_done = p_full + 2;
+  uint64_t* s_full = kv_empty + STAGES;  // [2] per query tile
+  uint64_t* p_full = s_full + 2;         // [2]
+  uint64_t* o_done = p_full + 2;         // [2]
   uint64_t* drain = o_done + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::oTmem);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + L::oAbort);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bh = blockIdx.y;
-  const int qt = CAUSAL ? (gridDim.x - 1 - blockIdx.x) : blockIdx.x;  // heavy tiles first
-  const int q0 = qt * BM;
+  const int cta = CAUSAL ? (gridDim.x - 1 - blockIdx.x) : blockIdx.x;  // heavy CTAs first
+  const int q0 = cta * (NQT * BM);
   int n_tiles = (M + BN - 1) / BN;
-  if (CAUSAL) n_tiles = min(n_tiles, (q0 + BM - 1) / BN + 1);
+  if (CAUSAL) n_tiles = min(n_tiles, (q0 + NQT * BM - 1) / BN + 1);
 
   if (threadIdx.x == 0) {
     tc::mbar_init(q_full, 1);
@@ -83,10 +85,10 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       tc::mbar_init(v_full + s, 1);
       tc::mbar_init(kv_empty + s, 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      tc::mbar_init(s_full + b, 1);
-      tc::mbar_init(p_full + b, 128);
-      tc::mbar_init(o_done + b, 1);
+    for (int t = 0; t < 2; ++t) {
+      tc::mbar_init(s_full + t, 1);
+      tc::mbar_init(p_full + t, 128);
+      tc::mbar_init(o_done + t, 1);
     }
     tc::mbar_init(drain, 1);
     *abort = 0;
@@ -97,7 +99,6 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t t_o = tmem + 256;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -106,9 +107,11 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       tc::prefetch_tmap(&tm_k);
       tc::prefetch_tmap(&tm_v);
       int issued = 0;
-      tc::mbar_expect_tx(q_full, L::kQ);
-      for (int cb = 0; cb < HD / 64; ++cb)
-        tc::tma_load_3d(smem + L::oQ + cb * BM * 128, &tm_q, q_full, cb * 64, q0, bh);
+      tc::mbar_expect_tx(q_full, NQT * L::kQ);
+      for (int t = 0; t < NQT; ++t)
+        for (int cb = 0; cb < HD / 64; ++cb)
+          tc::tma_load_3d(smem + L::oQ + t * L::kQ + cb * BM * 128, &tm_q, q_full, cb * 64,
+                          q0 + t * BM, bh);
       for (int j = 0; j < n_tiles; ++j) {
         const int st = j % STAGES;
         if (j >= STAGES && !tc::mbar_wait(kv_empty + st, ((j / STAGES) - 1) & 1, abort)) break;
@@ -136,80 +139,89 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       constexpr uint32_t id_s = tc::idesc_f16(BM, BN, tc::AbFmt<T>::v, 0, 0);
       constexpr uint32_t id_pv = tc::idesc_f16(BM, HD, tc::AbFmt<T>::v, 0, 1);
       const uint32_t q_addr = tc::smem_u32(smem + L::oQ);
-      auto issue_s = [&](int j) -> bool {
-        const int st = j % STAGES;
-        if (!tc::mbar_wait(k_full + st, (j / STAGES) & 1, abort)) return false;
-        tc::tc_fence_after();
-        const uint32_t k_addr = tc::smem_u32(smem + L::oK + st * L::kKV);
+      // S_t(j) = Q_t K_j^T into TMEM columns [128t, 128t+128)
+      auto issue_s = [&](int t, int j) {
+        const uint32_t k_addr = tc::smem_u32(smem + L::oK + (j % STAGES) * L::kKV);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t off_q = (kk / 4) * (BM * 128) + (kk % 4) * 32;
+          const uint32_t off_q = t * L::kQ + (kk / 4) * (BM * 128) + (kk % 4) * 32;
           const uint32_t off_k = (kk / 4) * (BN * 128) + (kk % 4) * 32;
-          tc::mma_ss(tmem + (j & 1) * 128, tc::sw128_desc(q_addr + off_q, 16, 1024),
+          tc::mma_ss(tmem + t * 128, tc::sw128_desc(q_addr + off_q, 16, 1024),
                      tc::sw128_desc(k_addr + off_k, 16, 1024), id_s, kk > 0 ? 1u : 0u);
         }
-        tc::mma_commit(s_full + (j & 1));
-        return true;
+        tc::mma_commit(s_full + t);
       };
-      bool ok = tc::mbar_wait(q_full, 0, abort);
-      if (ok) tc::tc_fence_after();
-      if (ok) ok = issue_s(0);
+      bool ok = tc::mbar_wait(q_full, 0, abort) && tc::mbar_wait(k_full, 0, abort);
+      if (ok) {
+        tc::tc_fence_after();
+        issue_s(0, 0);
+        issue_s(1, 0);
+      }
       for (int j = 0; ok && j < n_tiles; ++j) {
         const int st = j % STAGES;
-        if (j + 1 < n_tiles && !issue_s(j + 1)) break;
-        if (!tc::mbar_wait(p_full + (j & 1), (j >> 1) & 1, abort)) break;
-        if (!tc::mbar_wait(v_full + st, (j / STAGES) & 1, abort)) break;
-        tc::tc_fence_after();
-        const uint32_t p_addr = tc::smem_u32(smem + L::oP + (j & 1) * L::kP);
+        const bool more = j + 1 < n_tiles;
         const uint32_t v_addr = tc::smem_u32(smem + L::oV + st * L::kKV);
+        for (int t = 0; t < NQT; ++t) {
+          if (!tc::mbar_wait(p_full + t, j & 1, abort)) { ok = false; break; }
+          if (t == 0 && !tc::mbar_wait(v_full + st, (j / STAGES) & 1, abort)) { ok = false; break; }
+          tc::tc_fence_after();
+          // O_t += P_t V_j, P_t read from TMEM (packed pairs, 8 columns per 16 keys)
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint32_t off_p = (kk / 4) * (BM * 128) + (kk % 4) * 32;
-          tc::mma_ss(t_o, tc::sw128_desc(p_addr + off_p, 16, 1024),
-                     tc::sw128_desc(v_addr + kk * 16 * 128, BN * 128, 1024), id_pv,
-                     (j > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < BN / 16; ++kk)
+            tc::mma_ts(tmem + 256 + t * HD, tmem + t * 128 + kk * 8,
+                       tc::sw128_desc(v_addr + kk * 16 * 128, BN * 128, 1024), id_pv,
+                       (j > 0 || kk > 0) ? 1u : 0u);
+          if (!more) tc::mma_commit(o_done + t);
+          if (t == NQT - 1) tc::mma_commit(kv_empty + st);
+          if (more) {
+            if (t == 0) {
+              if (!tc::mbar_wait(k_full + (j + 1) % STAGES, ((j + 1) / STAGES) & 1, abort)) {
+                ok = false;
+                break;
+              }
+              tc::tc_fence_after();
+            }
+            issue_s(t, j + 1);
+          }
         }
-        tc::mma_commit(o_done + (j & 1));
-        tc::mma_commit(kv_empty + st);
       }
       // Every MMA issued above completes before TMEM is freed.
       tc::mma_commit(drain);
       tc::mbar_wait_drain(drain, 0);
     }
-  } else {
+  } else if (warp >= 4) {
     // ------------------------------------------------------------ softmax
+    const int t = (warp - 4) >> 2;       // query tile of this warp
     const int quarter = warp & 3;        // TMEM lanes this warp may access
     const int r = quarter * 32 + lane;   // row within the tile
-    const int row = q0 + r;
+    const int row = q0 + t * BM + r;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t t_s = tmem + t * 128 + lane_off;
+    const uint32_t t_o = tmem + 256 + t * HD + lane_off;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
-    // Waits are warp-uniform: the TMEM loads that follow are warp-collective.
+    // Waits are warp-uniform: the TMEM accesses that follow are warp-collective.
     auto wait = [&](uint64_t* bar, uint32_t parity) {
       return __all_sync(0xffffffffu, tc::mbar_wait(bar, parity, abort));
     };
     for (int j = 0; j < n_tiles; ++j) {
-      if (!wait(s_full + (j & 1), (j >> 1) & 1)) { ok = false; break; }
+      if (!wait(s_full + t, j & 1)) { ok = false; break; }
       tc::tc_fence_after();
-      float x[BN];
+      const int col0 = j * BN;
+      const bool edge = (col0 + BN > M) || (CAUSAL && col0 + BN - 1 > q0 + t * BM);
+      // pass 1: row maximum
+      float mt = -INFINITY;
 #pragma unroll
       for (int c = 0; c < BN / 32; ++c) {
         float v[32];
-        tc::tmem_ld32(tmem + (j & 1) * 128 + lane_off + c * 32, v);
+        tc::tmem_ld32(t_s + c * 32, v);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) x[c * 32 + i] = v[i] * scale_log2;
-      }
-      const int col0 = j * BN;
-      if ((col0 + BN > M) || (CAUSAL && col0 + BN - 1 > q0)) {
-#pragma unroll
-        for (int i = 0; i < BN; ++i) {
-          const int col = col0 + i;
-          if (col >= M || (CAUSAL && col > row)) x[i] = -INFINITY;
+        for (int i = 0; i < 32; ++i) {
+          const int col = col0 + c * 32 + i;
+          const bool keep = !edge || (col < M && (!CAUSAL || col <= row));
+          mt = fmaxf(mt, keep ? v[i] * scale_log2 : -INFINITY);
         }
       }
-      float mt = x[0];
-#pragma unroll
-      for (int i = 1; i < BN; ++i) mt = fmaxf(mt, x[i]);
       const float m_new = fmaxf(m, mt);
       float m_use = m;
       bool rescale = false;
@@ -219,51 +231,53 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
         m_use = m_new;
         rescale = true;
       }
-      const float m_sub = (m_use == -INFINITY) ? 0.f : m_use;
-      float rowsum = 0.f;
-#pragma unroll
-      for (int i = 0; i < BN; ++i) {
-        x[i] = tc::ex2(x[i] - m_sub);
-        rowsum += x[i];
-      }
       if (__any_sync(0xffffffffu, rescale)) {
-        // O holds PV_0..PV_{j-1}: wait for the last of them before touching it.
-        if (!wait(o_done + ((j - 1) & 1), ((j - 1) >> 1) & 1)) { ok = false; break; }
-        tc::tc_fence_after();
+        // O_t already holds PV_t(0..j-1), all complete (S_t(j) was issued after them).
         const float alpha = rescale ? tc::ex2(m - m_use) : 1.f;
         l *= alpha;
-#pragma unroll
+#pragma unroll 1
         for (int c = 0; c < HD / 32; ++c) {
           float v[32];
-          tc::tmem_ld32(t_o + lane_off + c * 32, v);
+          tc::tmem_ld32(t_o + c * 32, v);
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] *= alpha;
-          tc::tmem_st32(t_o + lane_off + c * 32, v);
+          tc::tmem_st32(t_o + c * 32, v);
         }
-        tc::tmem_wait_st();
+      }
+      m = m_use;
+      const float m_sub = (m_use == -INFINITY) ? 0.f : m_use;
+      // pass 2: P = exp2(s - m), written as packed pairs over S's first 64 columns
+      float rowsum = 0.f;
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        float v[32];
+        tc::tmem_ld32(t_s + c * 32, v);
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          float p0, p1;
+          {
+            const int col = col0 + c * 32 + i;
+            const bool keep = !edge || (col < M && (!CAUSAL || col <= row));
+            p0 = keep ? tc::ex2(v[i] * scale_log2 - m_sub) : 0.f;
+          }
+          {
+            const int col = col0 + c * 32 + i + 1;
+            const bool keep = !edge || (col < M && (!CAUSAL || col <= row));
+            p1 = keep ? tc::ex2(v[i + 1] * scale_log2 - m_sub) : 0.f;
+          }
+          rowsum += p0 + p1;
+          pk[i / 2] = tc::pack2<T>(p0, p1);
+        }
+        tc::tmem_st16(t_s + c * 16, pk);
       }
       l += rowsum;
-      m = m_use;
-      // P buffer (j & 1) was last read by PV_{j-2}.
-      if (j >= 2 && !wait(o_done + (j & 1), ((j - 2) >> 1) & 1)) { ok = false; break; }
-      const uint32_t p_addr = tc::smem_u32(smem + L::oP + (j & 1) * L::kP);
-#pragma unroll
-      for (int cb = 0; cb < BN / 64; ++cb) {
-#pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
-          const float* e = x + cb * 64 + ch * 8;
-          tc::st_shared_v4(p_addr + cb * (BM * 128) + tc::sw128_off(r, ch),
-                           tc::pack2<T>(e[0], e[1]), tc::pack2<T>(e[2], e[3]),
-                           tc::pack2<T>(e[4], e[5]), tc::pack2<T>(e[6], e[7]));
-        }
-      }
-      tc::fence_proxy_async_smem();
+      tc::tmem_wait_st();
       tc::tc_fence_before();
-      tc::mbar_arrive(p_full + (j & 1));
+      tc::mbar_arrive(p_full + t);
     }
     // ------------------------------------------------------------ epilogue
-    const int jl = n_tiles - 1;
-    if (ok && wait(o_done + (jl & 1), (jl >> 1) & 1)) {
+    if (ok && wait(o_done + t, 0)) {
       tc::tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       const bool store = row < Tq;
@@ -271,7 +285,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
 #pragma unroll
       for (int c = 0; c < HD / 32; ++c) {
         float v[32];
-        tc::tmem_ld32(t_o + lane_off + c * 32, v);  // warp-collective: before any branch
+        tc::tmem_ld32(t_o + c * 32, v);  // warp-collective: before any branch
         if (!store) continue;
         if (out_f32) {
           float4* dst = reinterpret_cast<float4*>(static_cast<float*>(out) + base + c * 32);

@@ -145,6 +145,32 @@ __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem]: A is M x 16 of packed 16-bit pairs, lane =
+// row, 8 consecutive 32-bit columns per instruction.
+__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                       uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+#define THERIA_U16R(i) "r"(v[i])
+// Warp-collective store of 16 consecutive 32-bit columns of this warp's lanes.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
+      "%13,%14,%15,%16};" ::"r"(taddr),
+      THERIA_U16R(0), THERIA_U16R(1), THERIA_U16R(2), THERIA_U16R(3), THERIA_U16R(4),
+      THERIA_U16R(5), THERIA_U16R(6), THERIA_U16R(7), THERIA_U16R(8), THERIA_U16R(9),
+      THERIA_U16R(10), THERIA_U16R(11), THERIA_U16R(12), THERIA_U16R(13), THERIA_U16R(14),
+      THERIA_U16R(15)
+      : "memory");
+}
+#undef THERIA_U16R
+
 // Arrive once on `bar` when every MMA this thread issued so far completes.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile(

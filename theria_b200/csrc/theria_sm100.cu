@@ -232,7 +232,8 @@ int tc_fwd_launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMa
   auto kern = tcfwd::fwd_kernel<T, HD, CAUSAL>;
   constexpr int smem = tcfwd::Smem<HD>::kAlloc;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  dim3 grid((unsigned)((s.T + tcfwd::BM - 1) / tcfwd::BM), (unsigned)(s.B * s.H));
+  dim3 grid((unsigned)((s.T + tcfwd::NQT * tcfwd::BM - 1) / (tcfwd::NQT * tcfwd::BM)),
+            (unsigned)(s.B * s.H));
   kern<<<grid, tcfwd::NTHREADS, smem, st>>>(mq, mk, mv, o, out_f32, lse, (int)s.T, (int)s.M,
                                             s.scale * 1.4426950408889634f);
   return launch_status();
