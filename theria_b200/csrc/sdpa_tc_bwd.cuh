@@ -3,8 +3,8 @@
 // Three launches per call:
 //   prep     z_i = rowsum(dO_i * O_i) and dQacc := 0        (memory bound)
 //   main     one CTA per (128-key tile, batch*head), looping over 64-row
-//            query tiles t (key/value-stationary), double-buffered so the
-//            tensor core works on tile t+1 while CUDA cores finish tile t:
+//            query tiles t (key/value-stationary), pipelined so the tensor
+//            core works on tile t+1 while CUDA cores finish tile t:
 //              S^T  = K Q_t^T,  dP^T = V dO_t^T      (tcgen05 -> TMEM)
 //              P^T  = exp(s S^T - LSE),  dS^T = P^T (dP^T - z)   (CUDA cores,
 //                     one key row per thread, 16-bit SW128 tiles in smem)
@@ -12,12 +12,12 @@
 //              dQ   = dS K, added to the fp32 accumulator dQacc with
 //                     global reductions; dK, dV are stored once at the end.
 //   finish   dQ = dQacc in the input dtype (dQacc is pre-scaled)
-// TMEM (512 columns): buffer b in {0,1} holds S^T at [128b, 128b+64) and
-// dP^T at [128b+64, 128b+128); dV at [256, 256+D); dK at [256+D, 256+2D).
-// dQ: for D = 128 as dQ^T = K^T dS^T (M = D = 128 lanes, 64 columns) written
-// over the S^T of its own buffer once the CUDA cores have read it; for D = 64
-// as dQ = dS K for a PAIR of query tiles at once (M = 128 query rows, the
-// two adjacent dS^T buffers read as one MN-major operand) into [384, 448).
+// TMEM (512 columns): S^T [0,64) and dP^T [64,128), released as soon as the
+// CUDA cores have loaded them; dV [128, 128+D); dK [128+D, 128+2D).
+// dQ: for D = 128 as dQ^T = K^T dS^T (M = D = 128 lanes, 64 columns) into a
+// double buffer [384 + 64b, 448 + 64b); for D = 64 as dQ = dS K for a PAIR of
+// query tiles at once (M = 128 query rows, the two adjacent dS^T buffers read
+// as one MN-major operand) into [256, 320).
 // Warp roles: warp 0 TMA, warp 1 MMA issuer + TMEM owner, warps 2..9 two
 // groups of four (one per TMEM lane quarter) splitting the columns.
 #pragma once
@@ -45,8 +45,8 @@ struct Smem {
   static constexpr int oP = oDO + 2 * kQ;   // 2 buffers
   static constexpr int oDS = oP + 2 * kP;   // 2 buffers (adjacent: a pair is one M=128 operand)
   static constexpr int oBar = oDS + 2 * kP;
-  // kv_full, q_full[2], q_empty[2], s_full[2], p_full[2], mma2_done[2],
-  // s_free[2], dq_free, drain
+  // kv_full, q_full[2], q_empty[2], s_full, s_read, p_full[2], mma2_done[2],
+  // dq_free[2], (spare), drain
   static constexpr int nBar = 1 + 2 * 6 + 2;
   static constexpr int oTmem = oBar + nBar * 8;
   static constexpr int oAbort = oTmem + 4;
@@ -109,11 +109,11 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
   uint64_t* kv_full = bars;
   uint64_t* q_full = bars + 1;      // [2] Q_t and dO_t landed
   uint64_t* q_empty = bars + 3;     // [2] stage free (MMAs reading it done)
-  uint64_t* s_full = bars + 5;      // [2] S^T, dP^T of the buffer computed
+  uint64_t* s_full = bars + 5;      // S^T, dP^T of the current tile computed
+  uint64_t* s_read = bars + 6;      // ... and loaded by the compute warps (256 arrivals)
   uint64_t* p_full = bars + 7;      // [2] P^T, dS^T of the buffer written (256 arrivals)
   uint64_t* mma2_done = bars + 9;   // [2] dV, dK (and dQ) MMAs of the tile done
-  uint64_t* s_free = bars + 11;     // [2] dQ^T read out of the buffer (256 arrivals)
-  uint64_t* dq_free = bars + 13;    // pair dQ read out (256 arrivals)
+  uint64_t* dq_free = bars + 11;    // [2] dQ of the buffer flushed (128 arrivals)
   uint64_t* drain = bars + 14;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::oTmem);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + L::oAbort);
@@ -130,12 +130,12 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
     for (int b = 0; b < 2; ++b) {
       tc::mbar_init(q_full + b, 1);
       tc::mbar_init(q_empty + b, 1);
-      tc::mbar_init(s_full + b, 1);
       tc::mbar_init(p_full + b, NCOMPUTE);
       tc::mbar_init(mma2_done + b, 1);
-      tc::mbar_init(s_free + b, NDQ);
+      tc::mbar_init(dq_free + b, NDQ);
     }
-    tc::mbar_init(dq_free, NDQ);
+    tc::mbar_init(s_full, 1);
+    tc::mbar_init(s_read, NCOMPUTE);
     tc::mbar_init(drain, 1);
     *abort = 0;
     tc::fence_barrier_init();
@@ -145,7 +145,9 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t t_dv = tmem + 256, t_dk = tmem + 256 + HD, t_dqp = tmem + 384;
+  // TMEM: S^T [0,64), dP^T [64,128), dV [128,128+D), dK [128+D,128+2D),
+  // dQ^T buffers [384+64b, 448+64b) (D=128) or the pair dQ [256,320) (D=64).
+  const uint32_t t_dv = tmem + 128, t_dk = tmem + 128 + HD, t_dqp = tmem + 256;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -189,28 +191,19 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       auto issue_s = [&](int t) -> bool {
         const int b = t & 1;
         if (!tc::mbar_wait(q_full + b, (t >> 1) & 1, abort)) return false;
+        // the single S^T/dP^T buffer is free once the previous tile was loaded
+        if (t >= 1 && !tc::mbar_wait(s_read, (t - 1) & 1, abort)) return false;
         tc::tc_fence_after();
-        const uint32_t ts = tmem + b * 128;
-        // dP^T first: its columns are free as soon as the tile two back was
-        // consumed; S^T's columns may still hold that tile's dQ^T.
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
           const uint32_t off_a = (kk / 4) * (BK * 128) + (kk % 4) * 32;
           const uint32_t off_b = b * L::kQ + (kk / 4) * (BQ * 128) + (kk % 4) * 32;
-          tc::mma_ss(ts + 64, tc::sw128_desc(a_v + off_a, 16, 1024),
+          tc::mma_ss(tmem + 64, tc::sw128_desc(a_v + off_a, 16, 1024),
                      tc::sw128_desc(a_do + off_b, 16, 1024), id_s, kk > 0 ? 1u : 0u);
-        }
-        if (!kPairDq && t >= 2 && !tc::mbar_wait(s_free + b, ((t - 2) >> 1) & 1, abort))
-          return false;
-        tc::tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t off_a = (kk / 4) * (BK * 128) + (kk % 4) * 32;
-          const uint32_t off_b = b * L::kQ + (kk / 4) * (BQ * 128) + (kk % 4) * 32;
-          tc::mma_ss(ts, tc::sw128_desc(a_k + off_a, 16, 1024),
+          tc::mma_ss(tmem, tc::sw128_desc(a_k + off_a, 16, 1024),
                      tc::sw128_desc(a_q + off_b, 16, 1024), id_s, kk > 0 ? 1u : 0u);
         }
-        tc::mma_commit(s_full + b);
+        tc::mma_commit(s_full);
         return true;
       };
       bool ok = tc::mbar_wait(kv_full, 0, abort);
@@ -232,10 +225,12 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
                      tc::sw128_desc(a_q + off_b, BQ * 128, 1024), id_kv, acc);
         }
         if constexpr (!kPairDq) {
-          // dQ^T = K^T dS^T over the keys, into this buffer's S^T columns
+          // dQ^T = K^T dS^T over the keys, into dQ^T buffer b
+          if (t >= 2 && !tc::mbar_wait(dq_free + b, ((t - 2) >> 1) & 1, abort)) break;
+          tc::tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk)
-            tc::mma_ss(tmem + b * 128, tc::sw128_desc(a_k + kk * 2048, BK * 128, 1024),
+            tc::mma_ss(tmem + 384 + b * 64, tc::sw128_desc(a_k + kk * 2048, BK * 128, 1024),
                        tc::sw128_desc(a_dsb + kk * 2048, BK * 128, 1024), id_dqt,
                        kk > 0 ? 1u : 0u);
         } else if ((t & 1) || t == n_iter - 1) {
@@ -278,6 +273,13 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       const int ql = q0 + grp * 32 + lane;
       const float my_l = ql < Tq ? __ldg(lse + row_base + ql) * 1.4426950408889634f : INFINITY;
       const float my_z = ql < Tq ? __ldg(z + row_base + ql) : 0.f;
+      if (!wait(s_full, t & 1)) { ok = false; break; }
+      tc::tc_fence_after();
+      float s[32], dp[32];
+      tc::tmem_ld32(tmem + lane_off + grp * 32, s);
+      tc::tmem_ld32(tmem + 64 + lane_off + grp * 32, dp);
+      tc::tc_fence_before();
+      tc::mbar_arrive(s_read);  // the tensor core may start on the next tile
       // P^T / dS^T buffer b is free once the MMAs that read it are done:
       // tile t-2's dV/dK (and dQ); with paired dQ, an even tile's buffer is
       // also read by the pair MMA issued with tile t-1.
@@ -285,11 +287,6 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
         const int tw = (kPairDq && !(t & 1)) ? t - 1 : t - 2;
         if (!wait(mma2_done + (tw & 1), (tw >> 1) & 1)) { ok = false; break; }
       }
-      if (!wait(s_full + b, (t >> 1) & 1)) { ok = false; break; }
-      tc::tc_fence_after();
-      float s[32], dp[32];
-      tc::tmem_ld32(tmem + b * 128 + lane_off + grp * 32, s);
-      tc::tmem_ld32(tmem + b * 128 + 64 + lane_off + grp * 32, dp);
       const bool diag = CAUSAL && (q0 < k0 + BK);
 #pragma unroll
       for (int e = 0; e < 32; ++e) {
@@ -373,7 +370,7 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
 #pragma unroll 1
         for (int c = 0; c < 2; ++c) {
           float v[32];
-          tc::tmem_ld32(tmem + (t & 1) * 128 + lane_off + c * 32, v);
+          tc::tmem_ld32(tmem + 384 + (t & 1) * 64 + lane_off + c * 32, v);
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
             const int q = qb + c * 32 + e;
@@ -381,7 +378,7 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
           }
         }
         tc::tc_fence_before();
-        tc::mbar_arrive(s_free + (t & 1));
+        tc::mbar_arrive(dq_free + (t & 1));
       } else {
         // dQ of the pair ending at tile t: lane = query row, 64 head dims
         const int q = (i_begin + (t & ~1)) * BQ + r;
