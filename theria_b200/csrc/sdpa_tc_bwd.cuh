@@ -36,18 +36,21 @@ constexpr int NTHREADS = 64 + NCOMPUTE + NDQ;
 template <int HD>
 struct Smem {
   static constexpr int kKV = BK * HD * 2;   // K or V tile
-  static constexpr int kQ = BQ * HD * 2;    // one Q or dO stage
+  static constexpr int kQ = BQ * HD * 2;    // one Q or dO tile
+  // Q/dO ring depth: a stage is released only when the tile's last MMAs
+  // complete, so the ring must cover that latency plus the TMA refill.
+  static constexpr int QST = HD == 128 ? 3 : 4;
   static constexpr int kP = BK * BQ * 2;    // one P^T or dS^T buffer [key][q]
   static constexpr int oK = 0;
   static constexpr int oV = oK + kKV;
-  static constexpr int oQ = oV + kKV;       // 2 stages
-  static constexpr int oDO = oQ + 2 * kQ;   // 2 stages
-  static constexpr int oP = oDO + 2 * kQ;   // 2 buffers
+  static constexpr int oQ = oV + kKV;       // QST stages
+  static constexpr int oDO = oQ + QST * kQ; // QST stages
+  static constexpr int oP = oDO + QST * kQ; // 2 buffers
   static constexpr int oDS = oP + 2 * kP;   // 2 buffers (adjacent: a pair is one M=128 operand)
   static constexpr int oBar = oDS + 2 * kP;
-  // kv_full, q_full[2], q_empty[2], s_full, s_read, p_full[2], mma2_done[2],
-  // dq_free[2], (spare), drain
-  static constexpr int nBar = 1 + 2 * 6 + 2;
+  // kv_full, q_full[4], q_empty[4], s_full, s_read, p_full[2], mma2_done[2],
+  // dq_free[2], drain
+  static constexpr int nBar = 1 + 8 + 2 + 6 + 1;
   static constexpr int oTmem = oBar + nBar * 8;
   static constexpr int oAbort = oTmem + 4;
   static constexpr int kBytes = oAbort + 4;
@@ -107,14 +110,15 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::oBar);
   uint64_t* kv_full = bars;
-  uint64_t* q_full = bars + 1;      // [2] Q_t and dO_t landed
-  uint64_t* q_empty = bars + 3;     // [2] stage free (MMAs reading it done)
-  uint64_t* s_full = bars + 5;      // S^T, dP^T of the current tile computed
-  uint64_t* s_read = bars + 6;      // ... and loaded by the compute warps (256 arrivals)
-  uint64_t* p_full = bars + 7;      // [2] P^T, dS^T of the buffer written (256 arrivals)
-  uint64_t* mma2_done = bars + 9;   // [2] dV, dK (and dQ) MMAs of the tile done
-  uint64_t* dq_free = bars + 11;    // [2] dQ of the buffer flushed (128 arrivals)
-  uint64_t* drain = bars + 14;
+  constexpr int QST = L::QST;
+  uint64_t* q_full = bars + 1;      // [QST] Q_t and dO_t landed
+  uint64_t* q_empty = bars + 5;     // [QST] stage free (MMAs reading it done)
+  uint64_t* s_full = bars + 9;      // S^T, dP^T of the current tile computed
+  uint64_t* s_read = bars + 10;     // ... and loaded by the compute warps (256 arrivals)
+  uint64_t* p_full = bars + 11;     // [2] P^T, dS^T of the buffer written (256 arrivals)
+  uint64_t* mma2_done = bars + 13;  // [2] dV, dK (and dQ) MMAs of the tile done
+  uint64_t* dq_free = bars + 15;    // [2] dQ of the buffer flushed (128 arrivals)
+  uint64_t* drain = bars + 17;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::oTmem);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + L::oAbort);
 
@@ -127,9 +131,11 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
 
   if (threadIdx.x == 0) {
     tc::mbar_init(kv_full, 1);
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < QST; ++b) {
       tc::mbar_init(q_full + b, 1);
       tc::mbar_init(q_empty + b, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
       tc::mbar_init(p_full + b, NCOMPUTE);
       tc::mbar_init(mma2_done + b, 1);
       tc::mbar_init(dq_free + b, NDQ);
@@ -161,21 +167,21 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       }
       int issued = 0;
       for (int t = 0; t < n_iter; ++t) {
-        const int b = t & 1;
-        if (t >= 2 && !tc::mbar_wait(q_empty + b, ((t - 2) >> 1) & 1, abort)) break;
+        const int st = t % QST;
+        if (t >= QST && !tc::mbar_wait(q_empty + st, ((t / QST) - 1) & 1, abort)) break;
         const int q0 = (i_begin + t) * BQ;
-        tc::mbar_expect_tx(q_full + b, 2 * L::kQ);
+        tc::mbar_expect_tx(q_full + st, 2 * L::kQ);
         for (int cb = 0; cb < HD / 64; ++cb) {
-          tc::tma_load_3d(smem + L::oQ + b * L::kQ + cb * BQ * 128, &tm_q, q_full + b, cb * 64,
-                          q0, bh);
-          tc::tma_load_3d(smem + L::oDO + b * L::kQ + cb * BQ * 128, &tm_do, q_full + b,
+          tc::tma_load_3d(smem + L::oQ + st * L::kQ + cb * BQ * 128, &tm_q, q_full + st,
+                          cb * 64, q0, bh);
+          tc::tma_load_3d(smem + L::oDO + st * L::kQ + cb * BQ * 128, &tm_do, q_full + st,
                           cb * 64, q0, bh);
         }
         issued = t + 1;
       }
       tc::mbar_wait_drain(kv_full, 0);
-      for (int t = issued > 2 ? issued - 2 : 0; t < issued; ++t)
-        tc::mbar_wait_drain(q_full + (t & 1), (t >> 1) & 1);
+      for (int t = issued > QST ? issued - QST : 0; t < issued; ++t)
+        tc::mbar_wait_drain(q_full + t % QST, (t / QST) & 1);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -189,15 +195,15 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       const uint32_t a_q = tc::smem_u32(smem + L::oQ), a_do = tc::smem_u32(smem + L::oDO);
       const uint32_t a_p = tc::smem_u32(smem + L::oP), a_ds = tc::smem_u32(smem + L::oDS);
       auto issue_s = [&](int t) -> bool {
-        const int b = t & 1;
-        if (!tc::mbar_wait(q_full + b, (t >> 1) & 1, abort)) return false;
+        const int st = t % QST;
+        if (!tc::mbar_wait(q_full + st, (t / QST) & 1, abort)) return false;
         // the single S^T/dP^T buffer is free once the previous tile was loaded
         if (t >= 1 && !tc::mbar_wait(s_read, (t - 1) & 1, abort)) return false;
         tc::tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
           const uint32_t off_a = (kk / 4) * (BK * 128) + (kk % 4) * 32;
-          const uint32_t off_b = b * L::kQ + (kk / 4) * (BQ * 128) + (kk % 4) * 32;
+          const uint32_t off_b = st * L::kQ + (kk / 4) * (BQ * 128) + (kk % 4) * 32;
           tc::mma_ss(tmem + 64, tc::sw128_desc(a_v + off_a, 16, 1024),
                      tc::sw128_desc(a_do + off_b, 16, 1024), id_s, kk > 0 ? 1u : 0u);
           tc::mma_ss(tmem, tc::sw128_desc(a_k + off_a, 16, 1024),
@@ -217,7 +223,7 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
 #pragma unroll
         for (int kk = 0; kk < BQ / 16; ++kk) {
           // contraction over the tile's queries: P^T / dS^T K-major, dO / Q MN-major
-          const uint32_t off_b = b * L::kQ + kk * 16 * 128;
+          const uint32_t off_b = (t % QST) * L::kQ + kk * 16 * 128;
           const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
           tc::mma_ss(t_dv, tc::sw128_desc(a_pb + kk * 32, 16, 1024),
                      tc::sw128_desc(a_do + off_b, BQ * 128, 1024), id_kv, acc);
@@ -245,7 +251,7 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
                        kk > 0 ? 1u : 0u);
         }
         tc::mma_commit(mma2_done + b);
-        tc::mma_commit(q_empty + b);
+        tc::mma_commit(q_empty + t % QST);
       }
       tc::mma_commit(drain);
       tc::mbar_wait_drain(drain, 0);
