@@ -339,6 +339,37 @@ def run_maml(args, world, rank, dev, steps=None):
             "theria_launches_per_step": launches / steps}
 
 
+def run_sweep(args, world, rank, dev):
+    """configs[4]: causal bf16, B=1, H=32, D in {64,128}, N in 512..16384;
+    heads sharded over the ranks (H/world each); fwd, fwd+bwd, JVP, HVP."""
+    from theria_b200.attention import ops
+    H = 32 // world
+    out = []
+    for D in (64, 128):
+        for N in (512, 1024, 2048, 4096, 8192, 16384):
+            gen = torch.Generator("cpu").manual_seed(rank)
+            q, k, v, w, tq, tk, tv = (randn((1, H, N, D), gen, torch.bfloat16, dev)
+                                      for _ in range(7))
+            o, lse = ops.forward(q, k, v, causal=True)
+            steps = 3 if N >= 8192 else 10
+            t_f, _ = timed(lambda: ops.forward(q, k, v, causal=True), steps, 3, world)
+            t_b, _ = timed(lambda: ops.backward(q, k, v, w, lse, o=o, causal=True), steps, 3,
+                           world)
+            t_j, _ = timed(lambda: ops.jvp(q, k, v, tq, tk, tv, lse, causal=True), steps, 3,
+                           world)
+            t_h, _ = timed(lambda: ops.hvp(q, k, v, w, lse, tq, tk, tv, causal=True), steps, 3,
+                           world)
+            f = lambda kind, ms: flops(kind, 1, 32, N, D, True) / (ms * 1e-3) / 1e12  # noqa: E731
+            out.append({"D": D, "N": N, "fwd_tflops": f("fwd", t_f),
+                        "fwdbwd_tflops": f("fwdbwd", t_f + t_b), "jvp_tflops": f("jvp", t_j),
+                        "hvp_tflops": f("hvp", t_h), "fwd_ms": t_f, "bwd_ms": t_b,
+                        "jvp_ms": t_j, "hvp_ms": t_h})
+            del q, k, v, w, tq, tk, tv, o, lse
+    torch.cuda.empty_cache()
+    return {"config": "configs[4] causal bf16 B=1 H=32 (heads sharded), fwd+bwd = fwd + bwd "
+                      "launch times", "points": out}
+
+
 # ------------------------------------------------------------------ arms
 METRIC = "SDPA fwd+bwd TFLOP/s (bf16, N=4096)"
 CONFIG = {"workload": "configs[1]: SDPA fwd+bwd, bf16, B=4 H=16 N=4096 D=128, non-causal, "
@@ -386,6 +417,8 @@ def theria_arm(args, world, rank, local):
     if not args.no_extra:
         extra["jvp_hvp"] = run_jvp_hvp(args, world, rank, dev)
         extra["maml"] = run_maml(args, world, rank, dev)
+        if args.sweep:
+            extra["long_seq_sweep"] = run_sweep(args, world, rank, dev)
         if not causal:
             c = run_fwdbwd(args, world, rank, dev, causal=True, with_e2e=False)
             extra["fwdbwd_causal"] = {"tflops": c["value"], "ms_per_step": c["ms_per_step"]}
@@ -454,6 +487,8 @@ def main():
     ap.add_argument("--impl", choices=["theria", "reference"], default="theria")
     ap.add_argument("--workload", choices=["fwdbwd", "fwdbwd_causal"], default="fwdbwd")
     ap.add_argument("--no-extra", action="store_true")
+    ap.add_argument("--sweep", action="store_true",
+                    help="add the configs[4] long-sequence causal sweep to `extra`")
     ap.add_argument("--cpu-budget", type=float, default=12.0,
                     help="seconds of CPU work for the cpu_baseline sample")
     ap.add_argument("--profile-case", choices=["fwdbwd", "jvp", "hvp"], default=None,
