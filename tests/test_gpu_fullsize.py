@@ -1,0 +1,89 @@
+"""Full benchmark sizes on the GPU, checked through properties that do not
+need the whole problem on the CPU: every (b, h) slice of the output depends
+only on that slice of the inputs, so selected slices are compared with the
+CPU oracle; plus linearity and symmetry identities of the whole operator.
+
+bf16 [4,16,4096,128] fwd+bwd (non-causal and causal);
+bf16 [2,8,2048,64] JVP and HVP.
+"""
+
+import pytest
+import torch
+
+from oracle import sdpa_oracle as orc
+from tests._util import max_abs
+
+pytestmark = pytest.mark.gpu
+if not torch.cuda.is_available():
+    pytest.skip("CUDA not available", allow_module_level=True)
+
+from theria_b200.attention import ops  # noqa: E402
+
+TOL = 2e-2  # bf16 max abs against the fp32 oracle
+
+
+def _draw(shape, n, seed):
+    g = torch.Generator("cpu").manual_seed(seed)
+    return [torch.randn(*shape, generator=g).to(torch.bfloat16) for _ in range(n)]
+
+
+def _slice(t, b, h):
+    return t[b:b + 1, h:h + 1].float().cpu()
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_cfg2_fwd_bwd_slices_match_oracle(causal):
+    shape = (4, 16, 4096, 128)
+    q, k, v, do = _draw(shape, 4, seed=0)
+    qd, kd, vd, dod = (t.cuda() for t in (q, k, v, do))
+    o, lse = ops.forward(qd, kd, vd, causal=causal)
+    dq, dk, dv = ops.backward(qd, kd, vd, dod, lse, o=o, causal=causal)
+    torch.cuda.synchronize()
+    for b, h in ((0, 0), (3, 15), (2, 7)):
+        qs, ks, vs, ds = (_slice(t, b, h) for t in (q, k, v, do))
+        assert max_abs(_slice(o, b, h), orc.attention(qs, ks, vs, causal=causal)) <= TOL
+        _, _, lse_ref = orc.row_stats(qs, ks, causal=causal)
+        assert max_abs(lse[b:b + 1, h:h + 1].cpu(), lse_ref) <= 1e-3
+        ref = orc.backward(qs, ks, vs, ds, causal=causal)
+        for x, r in zip((dq, dk, dv), ref):
+            assert max_abs(_slice(x, b, h), r) <= TOL
+
+
+def test_cfg2_forward_is_an_average_of_values():
+    # rows of P sum to one: V = c * ones gives O = c exactly (up to bf16 of c)
+    shape = (4, 16, 4096, 128)
+    q, k = _draw(shape, 2, seed=1)
+    v = torch.full(shape, 0.75, dtype=torch.bfloat16)
+    o, _ = ops.forward(q.cuda(), k.cuda(), v.cuda())
+    assert (o.float() - 0.75).abs().max().item() <= 4e-3
+
+
+def test_cfg3_jvp_hvp_slices_match_oracle():
+    shape = (2, 8, 2048, 64)
+    q, k, v, w, tq, tk, tv = _draw(shape, 7, seed=2)
+    dev = [t.cuda() for t in (q, k, v, w, tq, tk, tv)]
+    _, lse = ops.forward(*dev[:3])
+    ot = ops.jvp(dev[0], dev[1], dev[2], dev[4], dev[5], dev[6], lse)
+    hq, hk, hv, ot2 = ops.hvp(dev[0], dev[1], dev[2], dev[3], lse, dev[4], dev[5], dev[6])
+    torch.cuda.synchronize()
+    for b, h in ((0, 0), (1, 7)):
+        sl = [_slice(t, b, h) for t in (q, k, v, w, tq, tk, tv)]
+        assert max_abs(_slice(ot, b, h), orc.jvp(sl[0], sl[1], sl[2], sl[4], sl[5], sl[6])) <= TOL
+        ref = orc.hvp(*sl)
+        for x, r in zip((hq, hk, hv, ot2), ref):
+            assert max_abs(_slice(x, b, h), r) <= TOL
+
+
+def test_cfg3_hvp_is_symmetric_and_linear():
+    # <u2, H u1> == <u1, H u2> (H is a Hessian), and H(2u) == 2 H u.
+    shape = (2, 8, 2048, 64)
+    q, k, v, w, a1, b1, c1, a2, b2, c2 = (t.cuda() for t in _draw(shape, 10, seed=3))
+    _, lse = ops.forward(q, k, v)
+    h1 = ops.hvp(q, k, v, w, lse, a1, b1, c1)[:3]
+    h2 = ops.hvp(q, k, v, w, lse, a2, b2, c2)[:3]
+    s12 = sum((x.float() * y.float()).sum() for x, y in zip(h1, (a2, b2, c2))).item()
+    s21 = sum((x.float() * y.float()).sum() for x, y in zip(h2, (a1, b1, c1))).item()
+    assert abs(s12 - s21) <= 1e-2 * max(abs(s12), abs(s21))
+    h2x = ops.hvp(q, k, v, w, lse, 2 * a1, 2 * b1, 2 * c1)[:3]
+    for x, y in zip(h1, h2x):
+        assert (2 * x.float() - y.float()).abs().max().item() <= 4e-2
