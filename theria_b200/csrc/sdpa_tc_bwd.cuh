@@ -293,13 +293,18 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
         const int tw = (kPairDq && !(t & 1)) ? t - 1 : t - 2;
         if (!wait(mma2_done + (tw & 1), (tw >> 1) & 1)) { ok = false; break; }
       }
+      // Masking is needed only on the causal diagonal and for a ragged last
+      // key tile; the test is uniform per tile, so other tiles skip it.
       const bool diag = CAUSAL && (q0 < k0 + BK);
+      const bool edge = diag || (k0 + BK > M);
+      // valid columns e satisfy e >= e_min (causal: query >= key); none if key >= M
+      const int e_min = key >= M ? 32 : (diag ? key - (q0 + grp * 32) : 0);
 #pragma unroll
       for (int e = 0; e < 32; ++e) {
         const float lq = __shfl_sync(0xffffffffu, my_l, e);
         const float zq = __shfl_sync(0xffffffffu, my_z, e);
-        float p = tc::ex2(s[e] * scale_log2 - lq);  // rows past the end: lq = +inf -> 0
-        if (key >= M || (diag && q0 + grp * 32 + e < key)) p = 0.f;
+        float p = tc::ex2(fmaf(s[e], scale_log2, -lq));  // rows past the end: lq = +inf -> 0
+        if (edge && e < e_min) p = 0.f;
         s[e] = p;                   // P^T
         dp[e] = p * (dp[e] - zq);   // dS^T
       }

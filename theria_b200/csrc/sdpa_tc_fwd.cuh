@@ -208,20 +208,30 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       if (!wait(s_full + t, j & 1)) { ok = false; break; }
       tc::tc_fence_after();
       const int col0 = j * BN;
+      // Tiles that need masking (the causal diagonal, the ragged last key
+      // tile) take a separate, slower path; the test is uniform per tile.
       const bool edge = (col0 + BN > M) || (CAUSAL && col0 + BN - 1 > q0 + t * BM);
+      const int lim = CAUSAL ? min(M, row + 1) - col0 : M - col0;  // valid columns < lim
       // pass 1: row maximum
       float mt = -INFINITY;
+      if (!edge) {
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-        float v[32];
-        tc::tmem_ld32(t_s + c * 32, v);
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          tc::tmem_ld32(t_s + c * 32, v);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int col = col0 + c * 32 + i;
-          const bool keep = !edge || (col < M && (!CAUSAL || col <= row));
-          mt = fmaxf(mt, keep ? v[i] * scale_log2 : -INFINITY);
+          for (int i = 0; i < 32; ++i) mt = fmaxf(mt, v[i]);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          tc::tmem_ld32(t_s + c * 32, v);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) mt = fmaxf(mt, c * 32 + i < lim ? v[i] : -INFINITY);
         }
       }
+      mt *= scale_log2;
       const float m_new = fmaxf(m, mt);
       float m_use = m;
       bool rescale = false;
@@ -253,21 +263,18 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
         float v[32];
         tc::tmem_ld32(t_s + c * 32, v);
         uint32_t pk[16];
+        if (!edge) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = tc::ex2(fmaf(v[i], scale_log2, -m_sub));
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            v[i] = c * 32 + i < lim ? tc::ex2(fmaf(v[i], scale_log2, -m_sub)) : 0.f;
+        }
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
-          float p0, p1;
-          {
-            const int col = col0 + c * 32 + i;
-            const bool keep = !edge || (col < M && (!CAUSAL || col <= row));
-            p0 = keep ? tc::ex2(v[i] * scale_log2 - m_sub) : 0.f;
-          }
-          {
-            const int col = col0 + c * 32 + i + 1;
-            const bool keep = !edge || (col < M && (!CAUSAL || col <= row));
-            p1 = keep ? tc::ex2(v[i + 1] * scale_log2 - m_sub) : 0.f;
-          }
-          rowsum += p0 + p1;
-          pk[i / 2] = tc::pack2<T>(p0, p1);
+          rowsum += v[i] + v[i + 1];
+          pk[i / 2] = tc::pack2<T>(v[i], v[i + 1]);
         }
         tc::tmem_st16(t_s + c * 16, pk);
       }

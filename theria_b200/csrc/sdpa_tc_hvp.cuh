@@ -241,14 +241,16 @@ hvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       tc::tc_fence_before();
       tc::mbar_arrive(s_read);
       const bool diag = CAUSAL && (q0 < k0 + BK);
+      const bool edge = diag || (k0 + BK > M);  // uniform per tile
+      const int e_min = key >= M ? 32 : (diag ? key - (q0 + grp * 32) : 0);
 #pragma unroll
       for (int e = 0; e < 32; ++e) {
         const float lq = __shfl_sync(0xffffffffu, my_l, e);
         const float cq = __shfl_sync(0xffffffffu, my_c, e);
         const float zq = __shfl_sync(0xffffffffu, my_z, e);
         const float zdq = __shfl_sync(0xffffffffu, my_zd, e);
-        float p = tc::ex2(sv[e] * scale_log2 - lq);
-        if (key >= M || (diag && q0 + grp * 32 + e < key)) p = 0.f;
+        float p = tc::ex2(fmaf(sv[e], scale_log2, -lq));
+        if (edge && e < e_min) p = 0.f;
         const float pd = p * (sd[e] * scale - cq);
         const float g = dp[e] - zq;
         sv[e] = pd;                                  // Pd^T

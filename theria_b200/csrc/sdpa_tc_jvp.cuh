@@ -212,11 +212,13 @@ jvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       tc::tc_fence_before();
       tc::mbar_arrive(s_free);  // S / Sd columns may be overwritten by tile j+1
       const int col0 = j * BN + grp * HALF;
+      // masking only where a tile crosses the causal diagonal or the last key
+      const bool edge = (col0 + HALF > M) || (CAUSAL && col0 + HALF - 1 > q0);
+      const int lim = (CAUSAL ? min(M, row + 1) : M) - col0;  // valid: e < lim
 #pragma unroll
       for (int e = 0; e < HALF; ++e) {
-        const int col = col0 + e;
-        const bool valid = col < M && (!CAUSAL || col <= row);
-        const float p = valid ? tc::ex2(sv[e] * scale_log2 - lse2) : 0.f;
+        float p = tc::ex2(fmaf(sv[e], scale_log2, -lse2));
+        if (edge && e >= lim) p = 0.f;
         // c is summed from U as rounded for the MMA, so that OA - c OP
         // cancels consistently (a row with one key gives Odot = tV exactly).
         const float u = to_f32<T>(from_f32<T>(p * (sd[e] * scale)));
