@@ -29,7 +29,7 @@ constexpr int NTHREADS = 64 + NCOMPUTE + NDQ;
 
 template <int HD>
 struct Cfg {
-  static constexpr int ST = HD == 64 ? 2 : 1;  // Q/tQ/W ring depth (smem allows 2 at D=64)
+  static constexpr int ST = HD == 64 ? 3 : 1;  // Q/tQ/W ring depth (what smem allows)
   static constexpr int kKV = BK * HD * 2;
   static constexpr int kQ = BQ * HD * 2;
   static constexpr int kP = BK * BQ * 2;
@@ -40,9 +40,9 @@ struct Cfg {
   static constexpr int oDS = oPd + kP;           // dS^T  x NB (adjacent)
   static constexpr int oDSd = oDS + NB * kP;     // dSd^T x NB (adjacent)
   static constexpr int oBar = oDSd + NB * kP;
-  // kv_full, q_full[2], q_empty[2], s_full, s_read, p_full, mma2_done[2],
+  // kv_full, q_full[3], q_empty[3], s_full, s_read, p_full, mma2_done[2],
   // hq_free, drain
-  static constexpr int nBar = 12;
+  static constexpr int nBar = 14;
   static constexpr int oTmem = oBar + nBar * 8;
   static constexpr int oAbort = oTmem + 4;
   static constexpr int kAlloc = oAbort + 4 + 1024;
@@ -64,9 +64,9 @@ hvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::oBar);
-  uint64_t *kv_full = bars, *q_full = bars + 1, *q_empty = bars + 3, *s_full = bars + 5,
-           *s_read = bars + 6, *p_full = bars + 7, *mma2_done = bars + 8, *hq_free = bars + 10,
-           *drain = bars + 11;
+  uint64_t *kv_full = bars, *q_full = bars + 1, *q_empty = bars + 4, *s_full = bars + 7,
+           *s_read = bars + 8, *p_full = bars + 9, *mma2_done = bars + 10, *hq_free = bars + 12,
+           *drain = bars + 13;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::oTmem);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + C::oAbort);
 
@@ -79,11 +79,11 @@ hvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
 
   if (threadIdx.x == 0) {
     tc::mbar_init(kv_full, 1);
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < 3; ++b) {
       tc::mbar_init(q_full + b, 1);
       tc::mbar_init(q_empty + b, 1);
-      tc::mbar_init(mma2_done + b, 1);
     }
+    for (int b = 0; b < 2; ++b) tc::mbar_init(mma2_done + b, 1);
     tc::mbar_init(s_full, 1);
     tc::mbar_init(s_read, NCOMPUTE);
     tc::mbar_init(p_full, NCOMPUTE);
