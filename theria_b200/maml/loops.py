@@ -96,15 +96,29 @@ def meta_loss_batched(model: nn.Module, tasks: TaskBatch, *, inner_lr: float = 0
     ``model.forward_tasks(params, x)`` must accept parameters with a leading
     task axis.  Returns the mean (or sum / ``denom``) of the per-task query
     losses.
+
+    The fast weights of all tasks live in ONE tensor phi [n_tasks, n_params]
+    (the parameters concatenated), viewed per parameter through ``split``:
+    an inner SGD step is then a single update of phi, and its gradient one
+    concatenation, instead of a chain of small kernels per parameter.
     """
     nt = tasks.x_s.shape[0]
-    phi = OrderedDict((n, p.unsqueeze(0).expand(nt, *p.shape)) for n, p in model.named_parameters())
+    names = [n for n, _ in model.named_parameters()]
+    params = [p for _, p in model.named_parameters()]
+    shapes = [p.shape for p in params]
+    sizes = [p.numel() for p in params]
+    theta = torch.cat([p.reshape(-1) for p in params])
+    phi = theta.unsqueeze(0).expand(nt, theta.numel())
+
+    def views(flat):
+        return OrderedDict((n, c.view(nt, *shp))
+                           for n, c, shp in zip(names, flat.split(sizes, dim=1), shapes))
+
     for _ in range(inner_steps):
-        ls = _task_losses(model.forward_tasks(phi, tasks.x_s), tasks.y_s).sum()
-        grads = torch.autograd.grad(ls, tuple(phi.values()), create_graph=not fo,
-                                    retain_graph=True)
-        phi = OrderedDict((n, p - inner_lr * g) for (n, p), g in zip(phi.items(), grads))
-    lq = _task_losses(model.forward_tasks(phi, tasks.x_q), tasks.y_q)
+        ls = _task_losses(model.forward_tasks(views(phi), tasks.x_s), tasks.y_s).sum()
+        (g,) = torch.autograd.grad(ls, (phi,), create_graph=not fo, retain_graph=True)
+        phi = phi - inner_lr * g
+    lq = _task_losses(model.forward_tasks(views(phi), tasks.x_q), tasks.y_q)
     if reduction == "sum":
         return lq.sum() / (denom if denom is not None else 1)
     return lq.mean()
