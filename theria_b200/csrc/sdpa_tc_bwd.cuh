@@ -194,6 +194,15 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       const uint32_t a_k = tc::smem_u32(smem + L::oK), a_v = tc::smem_u32(smem + L::oV);
       const uint32_t a_q = tc::smem_u32(smem + L::oQ), a_do = tc::smem_u32(smem + L::oDO);
       const uint32_t a_p = tc::smem_u32(smem + L::oP), a_ds = tc::smem_u32(smem + L::oDS);
+      // base descriptors (K-major "k", MN-major "m"), advanced by constant adds
+      const uint64_t kK = tc::sw128_desc(a_k, 16, 1024), kV = tc::sw128_desc(a_v, 16, 1024);
+      const uint64_t kQ = tc::sw128_desc(a_q, 16, 1024), kDO = tc::sw128_desc(a_do, 16, 1024);
+      const uint64_t kP = tc::sw128_desc(a_p, 16, 1024), kDS = tc::sw128_desc(a_ds, 16, 1024);
+      const uint64_t mQ = tc::sw128_desc(a_q, BQ * 128, 1024);
+      const uint64_t mDO = tc::sw128_desc(a_do, BQ * 128, 1024);
+      const uint64_t mK = tc::sw128_desc(a_k, BK * 128, 1024);
+      const uint64_t mDS = tc::sw128_desc(a_ds, BK * 128, 1024);
+      const uint64_t mDSpair = tc::sw128_desc(a_ds, L::kP, 1024);
       auto issue_s = [&](int t) -> bool {
         const int st = t % QST;
         if (!tc::mbar_wait(q_full + st, (t / QST) & 1, abort)) return false;
@@ -204,10 +213,10 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
         for (int kk = 0; kk < HD / 16; ++kk) {
           const uint32_t off_a = (kk / 4) * (BK * 128) + (kk % 4) * 32;
           const uint32_t off_b = st * L::kQ + (kk / 4) * (BQ * 128) + (kk % 4) * 32;
-          tc::mma_ss(tmem + 64, tc::sw128_desc(a_v + off_a, 16, 1024),
-                     tc::sw128_desc(a_do + off_b, 16, 1024), id_s, kk > 0 ? 1u : 0u);
-          tc::mma_ss(tmem, tc::sw128_desc(a_k + off_a, 16, 1024),
-                     tc::sw128_desc(a_q + off_b, 16, 1024), id_s, kk > 0 ? 1u : 0u);
+          tc::mma_ss(tmem + 64, tc::desc_at(kV, off_a), tc::desc_at(kDO, off_b), id_s,
+                     kk > 0 ? 1u : 0u);
+          tc::mma_ss(tmem, tc::desc_at(kK, off_a), tc::desc_at(kQ, off_b), id_s,
+                     kk > 0 ? 1u : 0u);
         }
         tc::mma_commit(s_full);
         return true;
@@ -219,16 +228,14 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
         if (t + 1 < n_iter && !issue_s(t + 1)) break;
         if (!tc::mbar_wait(p_full + b, (t >> 1) & 1, abort)) break;
         tc::tc_fence_after();
-        const uint32_t a_pb = a_p + b * L::kP, a_dsb = a_ds + b * L::kP;
+        const uint32_t pbo = b * L::kP;  // this tile's P^T / dS^T buffer offset
 #pragma unroll
         for (int kk = 0; kk < BQ / 16; ++kk) {
           // contraction over the tile's queries: P^T / dS^T K-major, dO / Q MN-major
           const uint32_t off_b = (t % QST) * L::kQ + kk * 16 * 128;
           const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
-          tc::mma_ss(t_dv, tc::sw128_desc(a_pb + kk * 32, 16, 1024),
-                     tc::sw128_desc(a_do + off_b, BQ * 128, 1024), id_kv, acc);
-          tc::mma_ss(t_dk, tc::sw128_desc(a_dsb + kk * 32, 16, 1024),
-                     tc::sw128_desc(a_q + off_b, BQ * 128, 1024), id_kv, acc);
+          tc::mma_ss(t_dv, tc::desc_at(kP, pbo + kk * 32), tc::desc_at(mDO, off_b), id_kv, acc);
+          tc::mma_ss(t_dk, tc::desc_at(kDS, pbo + kk * 32), tc::desc_at(mQ, off_b), id_kv, acc);
         }
         if constexpr (!kPairDq) {
           // dQ^T = K^T dS^T over the keys, into dQ^T buffer b
@@ -236,9 +243,8 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
           tc::tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk)
-            tc::mma_ss(tmem + 384 + b * 64, tc::sw128_desc(a_k + kk * 2048, BK * 128, 1024),
-                       tc::sw128_desc(a_dsb + kk * 2048, BK * 128, 1024), id_dqt,
-                       kk > 0 ? 1u : 0u);
+            tc::mma_ss(tmem + 384 + b * 64, tc::desc_at(mK, kk * 2048),
+                       tc::desc_at(mDS, pbo + kk * 2048), id_dqt, kk > 0 ? 1u : 0u);
         } else if ((t & 1) || t == n_iter - 1) {
           // dQ for the pair (2p, 2p+1): both dS^T buffers as one M = 128 operand
           const int p = t >> 1;
@@ -246,9 +252,8 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
           tc::tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk)
-            tc::mma_ss(t_dqp, tc::sw128_desc(a_ds + kk * 2048, L::kP, 1024),
-                       tc::sw128_desc(a_k + kk * 2048, BK * 128, 1024), id_dqp,
-                       kk > 0 ? 1u : 0u);
+            tc::mma_ss(t_dqp, tc::desc_at(mDSpair, kk * 2048), tc::desc_at(mK, kk * 2048),
+                       id_dqp, kk > 0 ? 1u : 0u);
         }
         tc::mma_commit(mma2_done + b);
         tc::mma_commit(q_empty + t % QST);

@@ -138,17 +138,19 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
     if (lane == 0) {
       constexpr uint32_t id_s = tc::idesc_f16(BM, BN, tc::AbFmt<T>::v, 0, 0);
       constexpr uint32_t id_pv = tc::idesc_f16(BM, HD, tc::AbFmt<T>::v, 0, 1);
-      const uint32_t q_addr = tc::smem_u32(smem + L::oQ);
+      // base descriptors, advanced per instruction by constant adds
+      const uint64_t dq0 = tc::sw128_desc(tc::smem_u32(smem + L::oQ), 16, 1024);
+      const uint64_t dk0 = tc::sw128_desc(tc::smem_u32(smem + L::oK), 16, 1024);
+      const uint64_t dv0 = tc::sw128_desc(tc::smem_u32(smem + L::oV), BN * 128, 1024);
       // S_t(j) = Q_t K_j^T into TMEM columns [128t, 128t+128)
       auto issue_s = [&](int t, int j) {
-        const uint32_t k_addr = tc::smem_u32(smem + L::oK + (j % STAGES) * L::kKV);
+        const uint64_t dq = tc::desc_at(dq0, t * L::kQ);
+        const uint64_t dk = tc::desc_at(dk0, (j % STAGES) * L::kKV);
 #pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t off_q = t * L::kQ + (kk / 4) * (BM * 128) + (kk % 4) * 32;
-          const uint32_t off_k = (kk / 4) * (BN * 128) + (kk % 4) * 32;
-          tc::mma_ss(tmem + t * 128, tc::sw128_desc(q_addr + off_q, 16, 1024),
-                     tc::sw128_desc(k_addr + off_k, 16, 1024), id_s, kk > 0 ? 1u : 0u);
-        }
+        for (int kk = 0; kk < HD / 16; ++kk)
+          tc::mma_ss(tmem + t * 128, tc::desc_at(dq, (kk / 4) * (BM * 128) + (kk % 4) * 32),
+                     tc::desc_at(dk, (kk / 4) * (BN * 128) + (kk % 4) * 32), id_s,
+                     kk > 0 ? 1u : 0u);
         tc::mma_commit(s_full + t);
       };
       bool ok = tc::mbar_wait(q_full, 0, abort) && tc::mbar_wait(k_full, 0, abort);
@@ -160,7 +162,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       for (int j = 0; ok && j < n_tiles; ++j) {
         const int st = j % STAGES;
         const bool more = j + 1 < n_tiles;
-        const uint32_t v_addr = tc::smem_u32(smem + L::oV + st * L::kKV);
+        const uint64_t dv = tc::desc_at(dv0, st * L::kKV);
         for (int t = 0; t < NQT; ++t) {
           if (!tc::mbar_wait(p_full + t, j & 1, abort)) { ok = false; break; }
           if (t == 0 && !tc::mbar_wait(v_full + st, (j / STAGES) & 1, abort)) { ok = false; break; }
@@ -168,9 +170,8 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
           // O_t += P_t V_j, P_t read from TMEM (packed pairs, 8 columns per 16 keys)
 #pragma unroll
           for (int kk = 0; kk < BN / 16; ++kk)
-            tc::mma_ts(tmem + 256 + t * HD, tmem + t * 128 + kk * 8,
-                       tc::sw128_desc(v_addr + kk * 16 * 128, BN * 128, 1024), id_pv,
-                       (j > 0 || kk > 0) ? 1u : 0u);
+            tc::mma_ts(tmem + 256 + t * HD, tmem + t * 128 + kk * 8, tc::desc_at(dv, kk * 2048),
+                       id_pv, (j > 0 || kk > 0) ? 1u : 0u);
           if (!more) tc::mma_commit(o_done + t);
           if (t == NQT - 1) tc::mma_commit(kv_empty + st);
           if (more) {

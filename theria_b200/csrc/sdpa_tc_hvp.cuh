@@ -139,14 +139,26 @@ hvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       constexpr uint32_t id_hqp = tc::idesc_f16(2 * BQ, HD, ab, 1, 1);  // HD == 64
       const uint32_t a_k = tc::smem_u32(smem + C::oK), a_v = tc::smem_u32(smem + C::oV);
       const uint32_t a_tk = tc::smem_u32(smem + C::oTK), a_tv = tc::smem_u32(smem + C::oTV);
-      const uint32_t a_pd = tc::smem_u32(smem + C::oPd);
-      const uint32_t a_ds = tc::smem_u32(smem + C::oDS), a_dsd = tc::smem_u32(smem + C::oDSd);
+      const uint32_t a_q0 = tc::smem_u32(smem + C::oQ);
+      // base descriptors (K-major "k", MN-major "m"), advanced by constant adds
+      const uint64_t kK = tc::sw128_desc(a_k, 16, 1024), kV = tc::sw128_desc(a_v, 16, 1024);
+      const uint64_t kTK = tc::sw128_desc(a_tk, 16, 1024), kTV = tc::sw128_desc(a_tv, 16, 1024);
+      const uint64_t kQ0 = tc::sw128_desc(a_q0, 16, 1024);              // + stage, Q/tQ/W
+      const uint64_t mQ0 = tc::sw128_desc(a_q0, BQ * 128, 1024);
+      const uint64_t kPd = tc::sw128_desc(tc::smem_u32(smem + C::oPd), 16, 1024);
+      const uint64_t kDS = tc::sw128_desc(tc::smem_u32(smem + C::oDS), 16, 1024);
+      const uint64_t kDSd = tc::sw128_desc(tc::smem_u32(smem + C::oDSd), 16, 1024);
+      const uint64_t mK = tc::sw128_desc(a_k, BK * 128, 1024);
+      const uint64_t mTK = tc::sw128_desc(a_tk, BK * 128, 1024);
+      const uint64_t mDS = tc::sw128_desc(tc::smem_u32(smem + C::oDS), BK * 128, 1024);
+      const uint64_t mDSd = tc::sw128_desc(tc::smem_u32(smem + C::oDSd), BK * 128, 1024);
+      const uint64_t mDSp = tc::sw128_desc(tc::smem_u32(smem + C::oDS), C::kP, 1024);
+      const uint64_t mDSdp = tc::sw128_desc(tc::smem_u32(smem + C::oDSd), C::kP, 1024);
       bool ok = tc::mbar_wait(kv_full, 0, abort);
       for (int t = 0; ok && t < n_iter; ++t) {
         const int st = t % ST;
-        const int b = kPair ? (t & 1) : 0;
-        const uint32_t a_q = tc::smem_u32(smem + C::oQ + st * 3 * C::kQ);
-        const uint32_t a_tq = a_q + C::kQ, a_w = a_q + 2 * C::kQ;
+        const uint32_t bo = (kPair ? (t & 1) : 0) * C::kP;  // dS/dSd buffer offset
+        const uint32_t qo = st * 3 * C::kQ, to = qo + C::kQ, wo = qo + 2 * C::kQ;
         if (!tc::mbar_wait(q_full + st, (t / ST) & 1, abort)) break;
         if (t >= 1 && !tc::mbar_wait(s_read, (t - 1) & 1, abort)) break;
         if (!kPair && t >= 1 && !tc::mbar_wait(hq_free, (t - 1) & 1, abort)) break;
@@ -156,36 +168,34 @@ hvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
           const uint32_t oa = (kk / 4) * (BK * 128) + (kk % 4) * 32;
           const uint32_t ob = (kk / 4) * (BQ * 128) + (kk % 4) * 32;
           const uint32_t acc = kk > 0 ? 1u : 0u;
-          auto d = [](uint32_t a) { return tc::sw128_desc(a, 16, 1024); };
-          tc::mma_ss(tmem + 0, d(a_k + oa), d(a_q + ob), id_s, acc);      // S^T
-          tc::mma_ss(tmem + 64, d(a_k + oa), d(a_tq + ob), id_s, acc);    // Sd'^T
-          tc::mma_ss(tmem + 64, d(a_tk + oa), d(a_q + ob), id_s, 1u);
-          tc::mma_ss(tmem + 128, d(a_v + oa), d(a_w + ob), id_s, acc);    // dP^T
-          tc::mma_ss(tmem + 192, d(a_tv + oa), d(a_w + ob), id_s, acc);   // dPd^T
+          tc::mma_ss(tmem + 0, tc::desc_at(kK, oa), tc::desc_at(kQ0, qo + ob), id_s, acc);
+          tc::mma_ss(tmem + 64, tc::desc_at(kK, oa), tc::desc_at(kQ0, to + ob), id_s, acc);
+          tc::mma_ss(tmem + 64, tc::desc_at(kTK, oa), tc::desc_at(kQ0, qo + ob), id_s, 1u);
+          tc::mma_ss(tmem + 128, tc::desc_at(kV, oa), tc::desc_at(kQ0, wo + ob), id_s, acc);
+          tc::mma_ss(tmem + 192, tc::desc_at(kTV, oa), tc::desc_at(kQ0, wo + ob), id_s, acc);
         }
         tc::mma_commit(s_full);
         if (!tc::mbar_wait(p_full, t & 1, abort)) break;
         tc::tc_fence_after();
-        const uint32_t ds_b = a_ds + b * C::kP, dsd_b = a_dsd + b * C::kP;
 #pragma unroll
         for (int kk = 0; kk < BQ / 16; ++kk) {
           const uint32_t ob = kk * 16 * 128;
           const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
-          auto dk_ = [](uint32_t a) { return tc::sw128_desc(a, 16, 1024); };
-          auto dm = [](uint32_t a) { return tc::sw128_desc(a, BQ * 128, 1024); };
-          tc::mma_ss(t_hk, dk_(dsd_b + kk * 32), dm(a_q + ob), id_kv, acc);   // dSd^T Q
-          tc::mma_ss(t_hk, dk_(ds_b + kk * 32), dm(a_tq + ob), id_kv, 1u);    // dS^T tQ
-          tc::mma_ss(t_hv, dk_(a_pd + kk * 32), dm(a_w + ob), id_kv, acc);    // Pd^T W
+          tc::mma_ss(t_hk, tc::desc_at(kDSd, bo + kk * 32), tc::desc_at(mQ0, qo + ob), id_kv,
+                     acc);                                                         // dSd^T Q
+          tc::mma_ss(t_hk, tc::desc_at(kDS, bo + kk * 32), tc::desc_at(mQ0, to + ob), id_kv,
+                     1u);                                                          // dS^T tQ
+          tc::mma_ss(t_hv, tc::desc_at(kPd, kk * 32), tc::desc_at(mQ0, wo + ob), id_kv,
+                     acc);                                                         // Pd^T W
         }
         if constexpr (!kPair) {
           // hQ^T = K^T dSd^T + tK^T dS^T, into the S^T columns
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
             const uint32_t o = kk * 2048;
-            tc::mma_ss(tmem, tc::sw128_desc(a_k + o, BK * 128, 1024),
-                       tc::sw128_desc(dsd_b + o, BK * 128, 1024), id_hqt, kk > 0 ? 1u : 0u);
-            tc::mma_ss(tmem, tc::sw128_desc(a_tk + o, BK * 128, 1024),
-                       tc::sw128_desc(ds_b + o, BK * 128, 1024), id_hqt, 1u);
+            tc::mma_ss(tmem, tc::desc_at(mK, o), tc::desc_at(mDSd, bo + o), id_hqt,
+                       kk > 0 ? 1u : 0u);
+            tc::mma_ss(tmem, tc::desc_at(mTK, o), tc::desc_at(mDS, bo + o), id_hqt, 1u);
           }
         } else if ((t & 1) || t == n_iter - 1) {
           // hQ = dSd K + dS tK for the pair (2p, 2p+1)
@@ -195,10 +205,9 @@ hvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
             const uint32_t o = kk * 2048;
-            tc::mma_ss(t_hqp, tc::sw128_desc(a_dsd + o, C::kP, 1024),
-                       tc::sw128_desc(a_k + o, BK * 128, 1024), id_hqp, kk > 0 ? 1u : 0u);
-            tc::mma_ss(t_hqp, tc::sw128_desc(a_ds + o, C::kP, 1024),
-                       tc::sw128_desc(a_tk + o, BK * 128, 1024), id_hqp, 1u);
+            tc::mma_ss(t_hqp, tc::desc_at(mDSdp, o), tc::desc_at(mK, o), id_hqp,
+                       kk > 0 ? 1u : 0u);
+            tc::mma_ss(t_hqp, tc::desc_at(mDSp, o), tc::desc_at(mTK, o), id_hqp, 1u);
           }
         }
         tc::mma_commit(mma2_done + (t & 1));

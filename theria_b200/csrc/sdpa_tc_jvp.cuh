@@ -140,6 +140,11 @@ jvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       const uint32_t a_k = tc::smem_u32(smem + C::oK), a_tk = tc::smem_u32(smem + C::oTK);
       const uint32_t a_v = tc::smem_u32(smem + C::oV);
       const uint32_t a_p = tc::smem_u32(smem + C::oP), a_u = tc::smem_u32(smem + C::oU);
+      // base descriptors, advanced by constant adds
+      const uint64_t kQ = tc::sw128_desc(a_q, 16, 1024), kTQ = tc::sw128_desc(a_tq, 16, 1024);
+      const uint64_t kK = tc::sw128_desc(a_k, 16, 1024), kTK = tc::sw128_desc(a_tk, 16, 1024);
+      const uint64_t kP = tc::sw128_desc(a_p, 16, 1024), kU = tc::sw128_desc(a_u, 16, 1024);
+      const uint64_t mV = tc::sw128_desc(a_v, BN * 128, 1024);
       bool ok = tc::mbar_wait(q_full, 0, abort);
       for (int j = 0; ok && j < n_tiles; ++j) {
         if (!tc::mbar_wait(kt_full, j & 1, abort)) break;
@@ -150,12 +155,9 @@ jvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
           const uint32_t oq = (kk / 4) * (BM * 128) + (kk % 4) * 32;
           const uint32_t ok_ = (kk / 4) * (BN * 128) + (kk % 4) * 32;
           const uint32_t acc = kk > 0 ? 1u : 0u;
-          tc::mma_ss(tmem + C::tS, tc::sw128_desc(a_q + oq, 16, 1024),
-                     tc::sw128_desc(a_k + ok_, 16, 1024), id_s, acc);
-          tc::mma_ss(tmem + C::tSd, tc::sw128_desc(a_tq + oq, 16, 1024),
-                     tc::sw128_desc(a_k + ok_, 16, 1024), id_s, acc);
-          tc::mma_ss(tmem + C::tSd, tc::sw128_desc(a_q + oq, 16, 1024),
-                     tc::sw128_desc(a_tk + ok_, 16, 1024), id_s, 1u);
+          tc::mma_ss(tmem + C::tS, tc::desc_at(kQ, oq), tc::desc_at(kK, ok_), id_s, acc);
+          tc::mma_ss(tmem + C::tSd, tc::desc_at(kTQ, oq), tc::desc_at(kK, ok_), id_s, acc);
+          tc::mma_ss(tmem + C::tSd, tc::desc_at(kQ, oq), tc::desc_at(kTK, ok_), id_s, 1u);
         }
         tc::mma_commit(s_full);
         tc::mma_commit(kt_empty);
@@ -167,10 +169,8 @@ jvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
           const uint32_t oa = (kk / 4) * (BM * 128) + (kk % 4) * 32;
           const uint32_t ob = kk * 16 * 128;
           const uint32_t acc = (j > 0 || kk > 0) ? 1u : 0u;
-          tc::mma_ss(tmem + C::tOA, tc::sw128_desc(a_u + oa, 16, 1024),
-                     tc::sw128_desc(a_v + ob, BN * 128, 1024), id_a, acc);
-          tc::mma_ss(tmem + C::tOP, tc::sw128_desc(a_p + oa, 16, 1024),
-                     tc::sw128_desc(a_v + ob, BN * 128, 1024), id_pt, acc);
+          tc::mma_ss(tmem + C::tOA, tc::desc_at(kU, oa), tc::desc_at(mV, ob), id_a, acc);
+          tc::mma_ss(tmem + C::tOP, tc::desc_at(kP, oa), tc::desc_at(mV, ob), id_pt, acc);
         }
         tc::mma_commit(pv_done);
         tc::mma_commit(vt_empty);

@@ -235,6 +235,15 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo, uin
          ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
 }
 
+// The same descriptor with its start address moved by `bytes` (a multiple of
+// 16): the address field is the low 14 bits in 16-byte units, and shared
+// memory offsets stay far below 256 KB, so a plain add never carries out.
+// Kernels build each operand's base descriptor once and advance it per
+// instruction with this add, keeping the MMA issue loop short.
+__device__ __forceinline__ uint64_t desc_at(uint64_t base, uint32_t bytes) {
+  return base + (uint64_t)(bytes >> 4);
+}
+
 // Instruction descriptor of kind::f16 with an fp32 accumulator.
 // ab_bf16: 1 = bf16 operands, 0 = fp16.  a_mn/b_mn: 1 = MN-major operand.
 __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, int ab_bf16, int a_mn, int b_mn) {
