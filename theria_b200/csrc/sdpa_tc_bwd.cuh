@@ -7,20 +7,17 @@
 //            core works on tile t+1 while CUDA cores finish tile t:
 //              S^T  = K Q_t^T,  dP^T = V dO_t^T      (tcgen05 -> TMEM)
 //              P^T  = exp(s S^T - LSE),  dS^T = P^T (dP^T - z)   (CUDA cores,
-//                     one key row per thread; P^T to TMEM, dS^T to smem)
+//                     one key row per thread, 16-bit SW128 tiles in smem)
 //              dV  += P^T dO_t,  dK += dS^T Q_t       (TMEM accumulators)
 //              dQ   = dS K, added to the fp32 accumulator dQacc with
 //                     global reductions; dK, dV are stored once at the end.
 //   finish   dQ = dQacc in the input dtype (dQacc is pre-scaled)
 // TMEM (512 columns): S^T [0,64) and dP^T [64,128), released as soon as the
-// CUDA cores have loaded them; dV [128, 128+D); dK [128+D, 128+2D); P^T as
-// packed 16-bit pairs, double-buffered 32 columns each (the A operand of the
-// dV MMA, read from TMEM, so P never goes through shared memory) at
-// [448, 512) for D = 128 and [320, 384) for D = 64.
-// dQ: for D = 128 as dQ^T = K^T dS^T (M = D = 128 lanes, 64 columns) into
-// [384, 448); for D = 64 as dQ = dS K for a PAIR of query tiles at once
-// (M = 128 query rows, the two adjacent dS^T buffers read as one MN-major
-// operand) into [256, 320).
+// CUDA cores have loaded them; dV [128, 128+D); dK [128+D, 128+2D).
+// dQ: for D = 128 as dQ^T = K^T dS^T (M = D = 128 lanes, 64 columns) into a
+// double buffer [384 + 64b, 448 + 64b); for D = 64 as dQ = dS K for a PAIR of
+// query tiles at once (M = 128 query rows, the two adjacent dS^T buffers read
+// as one MN-major operand) into [256, 320).
 // Warp roles: warp 0 TMA, warp 1 MMA issuer + TMEM owner, warps 2..9 two
 // groups of four (one per TMEM lane quarter) splitting the columns.
 #pragma once
@@ -42,13 +39,14 @@ struct Smem {
   static constexpr int kQ = BQ * HD * 2;    // one Q or dO tile
   // Q/dO ring depth: a stage is released only when the tile's last MMAs
   // complete, so the ring must cover that latency plus the TMA refill.
-  static constexpr int QST = 4;
+  static constexpr int QST = HD == 128 ? 3 : 4;
   static constexpr int kP = BK * BQ * 2;    // one P^T or dS^T buffer [key][q]
   static constexpr int oK = 0;
   static constexpr int oV = oK + kKV;
   static constexpr int oQ = oV + kKV;       // QST stages
   static constexpr int oDO = oQ + QST * kQ; // QST stages
-  static constexpr int oDS = oDO + QST * kQ; // dS^T x2 (adjacent: a pair is one M=128 operand)
+  static constexpr int oP = oDO + QST * kQ; // 2 buffers
+  static constexpr int oDS = oP + 2 * kP;   // 2 buffers (adjacent: a pair is one M=128 operand)
   static constexpr int oBar = oDS + 2 * kP;
   // kv_full, q_full[4], q_empty[4], s_full, s_read, p_full[2], mma2_done[2],
   // dq_free[2], drain
@@ -156,8 +154,6 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
   // TMEM: S^T [0,64), dP^T [64,128), dV [128,128+D), dK [128+D,128+2D),
   // dQ^T buffers [384+64b, 448+64b) (D=128) or the pair dQ [256,320) (D=64).
   const uint32_t t_dv = tmem + 128, t_dk = tmem + 128 + HD, t_dqp = tmem + 256;
-  // P^T as packed 16-bit pairs (the A operand of dV), two buffers of 32 columns
-  const uint32_t t_pt = tmem + (HD == 128 ? 448 : 320);
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -197,11 +193,11 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       constexpr uint32_t id_dqp = tc::idesc_f16(2 * BQ, HD, ab, 1, 1);  // pair dQ (HD == 64)
       const uint32_t a_k = tc::smem_u32(smem + L::oK), a_v = tc::smem_u32(smem + L::oV);
       const uint32_t a_q = tc::smem_u32(smem + L::oQ), a_do = tc::smem_u32(smem + L::oDO);
-      const uint32_t a_ds = tc::smem_u32(smem + L::oDS);
+      const uint32_t a_p = tc::smem_u32(smem + L::oP), a_ds = tc::smem_u32(smem + L::oDS);
       // base descriptors (K-major "k", MN-major "m"), advanced by constant adds
       const uint64_t kK = tc::sw128_desc(a_k, 16, 1024), kV = tc::sw128_desc(a_v, 16, 1024);
       const uint64_t kQ = tc::sw128_desc(a_q, 16, 1024), kDO = tc::sw128_desc(a_do, 16, 1024);
-      const uint64_t kDS = tc::sw128_desc(a_ds, 16, 1024);
+      const uint64_t kP = tc::sw128_desc(a_p, 16, 1024), kDS = tc::sw128_desc(a_ds, 16, 1024);
       const uint64_t mQ = tc::sw128_desc(a_q, BQ * 128, 1024);
       const uint64_t mDO = tc::sw128_desc(a_do, BQ * 128, 1024);
       const uint64_t mK = tc::sw128_desc(a_k, BK * 128, 1024);
@@ -232,22 +228,22 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
         if (t + 1 < n_iter && !issue_s(t + 1)) break;
         if (!tc::mbar_wait(p_full + b, (t >> 1) & 1, abort)) break;
         tc::tc_fence_after();
-        const uint32_t pbo = b * L::kP;  // this tile's dS^T buffer offset
+        const uint32_t pbo = b * L::kP;  // this tile's P^T / dS^T buffer offset
 #pragma unroll
         for (int kk = 0; kk < BQ / 16; ++kk) {
           // contraction over the tile's queries: P^T / dS^T K-major, dO / Q MN-major
           const uint32_t off_b = (t % QST) * L::kQ + kk * 16 * 128;
           const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
-          tc::mma_ts(t_dv, t_pt + b * 32 + kk * 8, tc::desc_at(mDO, off_b), id_kv, acc);
+          tc::mma_ss(t_dv, tc::desc_at(kP, pbo + kk * 32), tc::desc_at(mDO, off_b), id_kv, acc);
           tc::mma_ss(t_dk, tc::desc_at(kDS, pbo + kk * 32), tc::desc_at(mQ, off_b), id_kv, acc);
         }
         if constexpr (!kPairDq) {
           // dQ^T = K^T dS^T over the keys, into dQ^T buffer b
-          if (t >= 1 && !tc::mbar_wait(dq_free, (t - 1) & 1, abort)) break;
+          if (t >= 2 && !tc::mbar_wait(dq_free + b, ((t - 2) >> 1) & 1, abort)) break;
           tc::tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk)
-            tc::mma_ss(tmem + 384, tc::desc_at(mK, kk * 2048),
+            tc::mma_ss(tmem + 384 + b * 64, tc::desc_at(mK, kk * 2048),
                        tc::desc_at(mDS, pbo + kk * 2048), id_dqt, kk > 0 ? 1u : 0u);
         } else if ((t & 1) || t == n_iter - 1) {
           // dQ for the pair (2p, 2p+1): both dS^T buffers as one M = 128 operand
@@ -278,7 +274,7 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
     auto wait = [&](uint64_t* bar, uint32_t parity) {
       return __all_sync(0xffffffffu, tc::mbar_wait(bar, parity, abort));
     };
-    const uint32_t a_ds = tc::smem_u32(smem + L::oDS);
+    const uint32_t a_p = tc::smem_u32(smem + L::oP), a_ds = tc::smem_u32(smem + L::oDS);
     const size_t row_base = (size_t)bh * Tq;
     for (int t = 0; t < n_iter; ++t) {
       const int b = t & 1;
@@ -317,21 +313,17 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
         s[e] = p;                   // P^T
         dp[e] = p * (dp[e] - zq);   // dS^T
       }
-      // P^T -> TMEM (packed pairs, this group's 16 columns of buffer b)
-      uint32_t pk[16];
-#pragma unroll
-      for (int e = 0; e < 32; e += 2) pk[e / 2] = tc::pack2<T>(s[e], s[e + 1]);
-      tc::tmem_st16(t_pt + b * 32 + grp * 16 + lane_off, pk);
-      // dS^T -> shared memory (B operand of dQ^T, A operand of dK)
-      const uint32_t db = a_ds + b * L::kP;
+      const uint32_t pb = a_p + b * L::kP, db = a_ds + b * L::kP;
 #pragma unroll
       for (int h = 0; h < 4; ++h) {
         const uint32_t off = tc::sw128_off(r, grp * 4 + h);
+        const float* pe = s + h * 8;
         const float* de = dp + h * 8;
+        tc::st_shared_v4(pb + off, tc::pack2<T>(pe[0], pe[1]), tc::pack2<T>(pe[2], pe[3]),
+                         tc::pack2<T>(pe[4], pe[5]), tc::pack2<T>(pe[6], pe[7]));
         tc::st_shared_v4(db + off, tc::pack2<T>(de[0], de[1]), tc::pack2<T>(de[2], de[3]),
                          tc::pack2<T>(de[4], de[5]), tc::pack2<T>(de[6], de[7]));
       }
-      tc::tmem_wait_st();
       tc::fence_proxy_async_smem();
       tc::tc_fence_before();
       tc::mbar_arrive(p_full + b);
@@ -394,7 +386,7 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
 #pragma unroll 1
         for (int c = 0; c < 2; ++c) {
           float v[32];
-          tc::tmem_ld32(tmem + 384 + lane_off + c * 32, v);
+          tc::tmem_ld32(tmem + 384 + (t & 1) * 64 + lane_off + c * 32, v);
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
             const int q = qb + c * 32 + e;
@@ -402,7 +394,7 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
           }
         }
         tc::tc_fence_before();
-        tc::mbar_arrive(dq_free);
+        tc::mbar_arrive(dq_free + (t & 1));
       } else {
         // dQ of the pair ending at tile t: lane = query row, 64 head dims
         const int q = (i_begin + (t & ~1)) * BQ + r;
