@@ -213,20 +213,26 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       // tile) take a separate, slower path; the test is uniform per tile.
       const bool edge = (col0 + BN > M) || (CAUSAL && col0 + BN - 1 > q0 + t * BM);
       const int lim = CAUSAL ? min(M, row + 1) - col0 : M - col0;  // valid columns < lim
-      // pass 1: row maximum (64-column TMEM loads: one wait per 64 scores)
-      float mt = -INFINITY;
+      // pass 1: row maximum (64-column TMEM loads; 8 independent partial
+      // maxima so the reduction is not one 128-long dependent chain)
+      float mp[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mp[i] = -INFINITY;
 #pragma unroll
       for (int c = 0; c < BN / 64; ++c) {
         float v[64];
         tc::tmem_ld64(t_s + c * 64, v);
         if (!edge) {
 #pragma unroll
-          for (int i = 0; i < 64; ++i) mt = fmaxf(mt, v[i]);
+          for (int i = 0; i < 64; ++i) mp[i & 7] = fmaxf(mp[i & 7], v[i]);
         } else {
 #pragma unroll
-          for (int i = 0; i < 64; ++i) mt = fmaxf(mt, c * 64 + i < lim ? v[i] : -INFINITY);
+          for (int i = 0; i < 64; ++i)
+            mp[i & 7] = fmaxf(mp[i & 7], c * 64 + i < lim ? v[i] : -INFINITY);
         }
       }
+      float mt = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
+                       fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
       mt *= scale_log2;
       const float m_new = fmaxf(m, mt);
       float m_use = m;
@@ -253,7 +259,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       m = m_use;
       const float m_sub = (m_use == -INFINITY) ? 0.f : m_use;
       // pass 2: P = exp2(s - m), written as packed pairs over S's first 64 columns
-      float rowsum = 0.f;
+      float rs[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // partial row sums
 #pragma unroll
       for (int c = 0; c < BN / 64; ++c) {
         float v[64];
@@ -269,12 +275,12 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
         uint32_t pk[32];
 #pragma unroll
         for (int i = 0; i < 64; i += 2) {
-          rowsum += v[i] + v[i + 1];
+          rs[(i / 2) & 7] += v[i] + v[i + 1];
           pk[i / 2] = tc::pack2<T>(v[i], v[i + 1]);
         }
         tc::tmem_st32u(t_s + c * 32, pk);
       }
-      l += rowsum;
+      l += ((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7]));
       tc::tmem_wait_st();
       tc::tc_fence_before();
       tc::mbar_arrive(p_full + t);
