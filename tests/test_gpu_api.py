@@ -181,3 +181,16 @@ def test_double_backward_through_strided_views():
     (hc,) = torch.autograd.grad((gc * tq.double()).sum(), (xc,))
     assert max_rel(gx, gc) <= 1e-5
     assert max_rel(hx, hc) <= 1e-4
+
+
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("shape", [(2, 2, 64, 32), (1, 2, 200, 64)])
+def test_forward_mode_ad_uses_the_jvp_kernel(causal, shape):
+    import torch.autograd.forward_ad as fwAD
+    q, k, v, tq, tk, tv = _qkv(shape, n=6, seed=8)
+    with fwAD.dual_level():
+        duals = [fwAD.make_dual(x.to(DEV), t.to(DEV)) for x, t in ((q, tq), (k, tk), (v, tv))]
+        out = sdpa(*duals, causal=causal)
+        primal, tangent = fwAD.unpack_dual(out)
+    assert max_rel(primal, orc.attention(q, k, v, causal=causal)) <= 1e-5
+    assert max_rel(tangent, orc.jvp(q, k, v, tq, tk, tv, causal=causal)) <= 1e-5

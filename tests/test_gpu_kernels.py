@@ -82,6 +82,8 @@ SHAPES = [
     (1, 1, 200, 200, 48),  # head dim off the tensor-core list
     (1, 2, 384, 640, 64),  # several key/query tiles, T < M
     (1, 2, 640, 384, 128), # T > M: keys past every causal query row
+    (1, 2, 20, 50, 16),    # whole-head kernels, T != M
+    (2, 1, 64, 33, 20),    # whole-head kernels, odd head dim
 ]
 DTYPES = [torch.float32, torch.bfloat16, torch.float16]
 

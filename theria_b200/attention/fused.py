@@ -71,8 +71,19 @@ class SDPAFunction(torch.autograd.Function):
         o, lse = ops.forward(q.contiguous(), k.contiguous(), v.contiguous(), causal=causal,
                              scale=scale)
         ctx.save_for_backward(q, k, v, o, lse)
+        ctx.save_for_forward(q, k, v, lse)
         ctx.causal, ctx.scale = causal, scale
         return o
+
+    @staticmethod
+    def jvp(ctx, tq, tk, tv, _causal=None, _scale=None):
+        """Forward-mode rule (torch.autograd.forward_ad): the JVP kernel."""
+        q, k, v, lse = ctx.saved_tensors
+        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+        tq = torch.zeros_like(q) if tq is None else _c(tq, q.dtype)
+        tk = torch.zeros_like(k) if tk is None else _c(tk, k.dtype)
+        tv = torch.zeros_like(v) if tv is None else _c(tv, v.dtype)
+        return ops.jvp(q, k, v, tq, tk, tv, lse, causal=ctx.causal, scale=ctx.scale)
 
     @staticmethod
     def backward(ctx, grad_out):
