@@ -36,90 +36,159 @@ __device__ __forceinline__ void load_mat(float* dst, const T* __restrict__ src, 
   }
 }
 
-// C[i][j] = alpha * sum_d A[i][d] B[j][d]   (A: [rA][D], B: [rB][D])
+// The products below give each thread 2 x 2 blocks of outputs, so every
+// shared-memory value loaded feeds two FMAs (the single-output form was
+// bound by shared-memory loads).  Odd extents are handled by clamping the
+// second row/column to the first and not storing it.
+
+// C[i][j] = alpha * (sum_d A1[i][d] B1[j][d] [+ A2[i][d] B2[j][d]])
+template <bool TWO>
+__device__ __forceinline__ void abt_impl(float* C, int ldc, const float* A1, const float* B1,
+                                         const float* A2, const float* B2, int rA, int rB,
+                                         int D, float alpha) {
+  const int nbj = (rB + 1) >> 1, nb = ((rA + 1) >> 1) * nbj;
+  for (int e = threadIdx.x; e < nb; e += blockDim.x) {
+    const int i0 = 2 * (e / nbj), j0 = 2 * (e % nbj);
+    const int i1 = min(i0 + 1, rA - 1), j1 = min(j0 + 1, rB - 1);
+    float c00 = 0.f, c01 = 0.f, c10 = 0.f, c11 = 0.f;
+    {
+      const float *a0 = A1 + i0 * (D + 1), *a1 = A1 + i1 * (D + 1);
+      const float *b0 = B1 + j0 * (D + 1), *b1 = B1 + j1 * (D + 1);
+      for (int d = 0; d < D; ++d) {
+        c00 = fmaf(a0[d], b0[d], c00);
+        c01 = fmaf(a0[d], b1[d], c01);
+        c10 = fmaf(a1[d], b0[d], c10);
+        c11 = fmaf(a1[d], b1[d], c11);
+      }
+    }
+    if (TWO) {
+      const float *a0 = A2 + i0 * (D + 1), *a1 = A2 + i1 * (D + 1);
+      const float *b0 = B2 + j0 * (D + 1), *b1 = B2 + j1 * (D + 1);
+      for (int d = 0; d < D; ++d) {
+        c00 = fmaf(a0[d], b0[d], c00);
+        c01 = fmaf(a0[d], b1[d], c01);
+        c10 = fmaf(a1[d], b0[d], c10);
+        c11 = fmaf(a1[d], b1[d], c11);
+      }
+    }
+    C[i0 * ldc + j0] = alpha * c00;
+    if (j0 + 1 < rB) C[i0 * ldc + j0 + 1] = alpha * c01;
+    if (i0 + 1 < rA) {
+      C[(i0 + 1) * ldc + j0] = alpha * c10;
+      if (j0 + 1 < rB) C[(i0 + 1) * ldc + j0 + 1] = alpha * c11;
+    }
+  }
+}
+
 __device__ __forceinline__ void abt(float* C, int ldc, const float* A, const float* B, int rA,
                                     int rB, int D, float alpha) {
-  for (int e = threadIdx.x; e < rA * rB; e += blockDim.x) {
-    const int i = e / rB, j = e - i * rB;
-    const float* a = A + i * (D + 1);
-    const float* b = B + j * (D + 1);
-    float acc = 0.f;
-    for (int d = 0; d < D; ++d) acc = fmaf(a[d], b[d], acc);
-    C[i * ldc + j] = alpha * acc;
-  }
+  abt_impl<false>(C, ldc, A, B, nullptr, nullptr, rA, rB, D, alpha);
 }
-
-// out[i][d] = alpha * sum_j S[i][j] X[j][d]       (S: [rS][cS] ld lds, X: [cS][D])
-template <typename OT>
-__device__ __forceinline__ void sx(OT* __restrict__ out, const float* S, int lds, const float* X,
-                                   int rS, int cS, int D, float alpha) {
-  for (int e = threadIdx.x; e < rS * D; e += blockDim.x) {
-    const int i = e / D, d = e - i * D;
-    float acc = 0.f;
-    for (int j = 0; j < cS; ++j) acc = fmaf(S[i * lds + j], X[j * (D + 1) + d], acc);
-    out[e] = from_f32<OT>(alpha * acc);
-  }
-}
-
-// out[j][d] = alpha * sum_i S[i][j] X[i][d]       (transpose of S)
-template <typename OT>
-__device__ __forceinline__ void stx(OT* __restrict__ out, const float* S, int lds,
-                                    const float* X, int rS, int cS, int D, float alpha) {
-  for (int e = threadIdx.x; e < cS * D; e += blockDim.x) {
-    const int j = e / D, d = e - j * D;
-    float acc = 0.f;
-    for (int i = 0; i < rS; ++i) acc = fmaf(S[i * lds + j], X[i * (D + 1) + d], acc);
-    out[e] = from_f32<OT>(alpha * acc);
-  }
-}
-
-// out[i][d] = alpha * sum_j (S1[i][j] X1[j][d] + S2[i][j] X2[j][d])
-template <typename OT>
-__device__ __forceinline__ void sx2(OT* __restrict__ out, const float* S1, const float* X1,
-                                    const float* S2, const float* X2, int lds, int rS, int cS,
-                                    int D, float alpha) {
-  for (int e = threadIdx.x; e < rS * D; e += blockDim.x) {
-    const int i = e / D, d = e - i * D;
-    float acc = 0.f;
-    for (int j = 0; j < cS; ++j) {
-      acc = fmaf(S1[i * lds + j], X1[j * (D + 1) + d], acc);
-      acc = fmaf(S2[i * lds + j], X2[j * (D + 1) + d], acc);
-    }
-    out[e] = from_f32<OT>(alpha * acc);
-  }
-}
-
-// out[j][d] = alpha * sum_i (S1[i][j] X1[i][d] + S2[i][j] X2[i][d])
-template <typename OT>
-__device__ __forceinline__ void stx2(OT* __restrict__ out, const float* S1, const float* X1,
-                                     const float* S2, const float* X2, int lds, int rS, int cS,
-                                     int D, float alpha) {
-  for (int e = threadIdx.x; e < cS * D; e += blockDim.x) {
-    const int j = e / D, d = e - j * D;
-    float acc = 0.f;
-    for (int i = 0; i < rS; ++i) {
-      acc = fmaf(S1[i * lds + j], X1[i * (D + 1) + d], acc);
-      acc = fmaf(S2[i * lds + j], X2[i * (D + 1) + d], acc);
-    }
-    out[e] = from_f32<OT>(alpha * acc);
-  }
-}
-
-__device__ __forceinline__ bool masked(int i, int j, int causal) { return causal && j > i; }
 
 // C = alpha * (A1 B1^T + A2 B2^T)
 __device__ __forceinline__ void abt2(float* C, int ldc, const float* A1, const float* B1,
                                      const float* A2, const float* B2, int rA, int rB, int D,
                                      float alpha) {
-  for (int e = threadIdx.x; e < rA * rB; e += blockDim.x) {
-    const int i = e / rB, j = e - i * rB;
-    const float *a1 = A1 + i * (D + 1), *b1 = B1 + j * (D + 1);
-    const float *a2 = A2 + i * (D + 1), *b2 = B2 + j * (D + 1);
-    float acc = 0.f;
-    for (int d = 0; d < D; ++d) acc = fmaf(a1[d], b1[d], fmaf(a2[d], b2[d], acc));
-    C[i * ldc + j] = alpha * acc;
+  abt_impl<true>(C, ldc, A1, B1, A2, B2, rA, rB, D, alpha);
+}
+
+template <typename OT>
+__device__ __forceinline__ void store2x2(OT* out, int ldo, int i0, int d0, int nI, int nD,
+                                         float alpha, float c00, float c01, float c10,
+                                         float c11) {
+  out[i0 * ldo + d0] = from_f32<OT>(alpha * c00);
+  if (d0 + 1 < nD) out[i0 * ldo + d0 + 1] = from_f32<OT>(alpha * c01);
+  if (i0 + 1 < nI) {
+    out[(i0 + 1) * ldo + d0] = from_f32<OT>(alpha * c10);
+    if (d0 + 1 < nD) out[(i0 + 1) * ldo + d0 + 1] = from_f32<OT>(alpha * c11);
   }
 }
+
+// out[i][d] = alpha * sum_j (S1[i][j] X1[j][d] [+ S2[i][j] X2[j][d]])
+//   (S: [rS][cS] at stride lds; X: [cS][D]; out: [rS][D] dense)
+template <bool TWO, typename OT>
+__device__ __forceinline__ void sx_impl(OT* __restrict__ out, const float* S1, const float* X1,
+                                        const float* S2, const float* X2, int lds, int rS,
+                                        int cS, int D, float alpha) {
+  const int nbd = (D + 1) >> 1, nb = ((rS + 1) >> 1) * nbd;
+  for (int e = threadIdx.x; e < nb; e += blockDim.x) {
+    const int i0 = 2 * (e / nbd), d0 = 2 * (e % nbd);
+    const int i1 = min(i0 + 1, rS - 1), d1 = min(d0 + 1, D - 1);
+    float c00 = 0.f, c01 = 0.f, c10 = 0.f, c11 = 0.f;
+    for (int j = 0; j < cS; ++j) {
+      const float s0 = S1[i0 * lds + j], s1 = S1[i1 * lds + j];
+      const float x0 = X1[j * (D + 1) + d0], x1 = X1[j * (D + 1) + d1];
+      c00 = fmaf(s0, x0, c00);
+      c01 = fmaf(s0, x1, c01);
+      c10 = fmaf(s1, x0, c10);
+      c11 = fmaf(s1, x1, c11);
+      if (TWO) {
+        const float t0 = S2[i0 * lds + j], t1 = S2[i1 * lds + j];
+        const float y0 = X2[j * (D + 1) + d0], y1 = X2[j * (D + 1) + d1];
+        c00 = fmaf(t0, y0, c00);
+        c01 = fmaf(t0, y1, c01);
+        c10 = fmaf(t1, y0, c10);
+        c11 = fmaf(t1, y1, c11);
+      }
+    }
+    store2x2(out, D, i0, d0, rS, D, alpha, c00, c01, c10, c11);
+  }
+}
+
+// out[j][d] = alpha * sum_i (S1[i][j] X1[i][d] [+ S2[i][j] X2[i][d]])  (S transposed)
+template <bool TWO, typename OT>
+__device__ __forceinline__ void stx_impl(OT* __restrict__ out, const float* S1, const float* X1,
+                                         const float* S2, const float* X2, int lds, int rS,
+                                         int cS, int D, float alpha) {
+  const int nbd = (D + 1) >> 1, nb = ((cS + 1) >> 1) * nbd;
+  for (int e = threadIdx.x; e < nb; e += blockDim.x) {
+    const int j0 = 2 * (e / nbd), d0 = 2 * (e % nbd);
+    const int j1 = min(j0 + 1, cS - 1), d1 = min(d0 + 1, D - 1);
+    float c00 = 0.f, c01 = 0.f, c10 = 0.f, c11 = 0.f;
+    for (int i = 0; i < rS; ++i) {
+      const float s0 = S1[i * lds + j0], s1 = S1[i * lds + j1];
+      const float x0 = X1[i * (D + 1) + d0], x1 = X1[i * (D + 1) + d1];
+      c00 = fmaf(s0, x0, c00);
+      c01 = fmaf(s0, x1, c01);
+      c10 = fmaf(s1, x0, c10);
+      c11 = fmaf(s1, x1, c11);
+      if (TWO) {
+        const float t0 = S2[i * lds + j0], t1 = S2[i * lds + j1];
+        const float y0 = X2[i * (D + 1) + d0], y1 = X2[i * (D + 1) + d1];
+        c00 = fmaf(t0, y0, c00);
+        c01 = fmaf(t0, y1, c01);
+        c10 = fmaf(t1, y0, c10);
+        c11 = fmaf(t1, y1, c11);
+      }
+    }
+    store2x2(out, D, j0, d0, cS, D, alpha, c00, c01, c10, c11);
+  }
+}
+
+template <typename OT>
+__device__ __forceinline__ void sx(OT* __restrict__ out, const float* S, int lds, const float* X,
+                                   int rS, int cS, int D, float alpha) {
+  sx_impl<false>(out, S, X, nullptr, nullptr, lds, rS, cS, D, alpha);
+}
+template <typename OT>
+__device__ __forceinline__ void sx2(OT* __restrict__ out, const float* S1, const float* X1,
+                                    const float* S2, const float* X2, int lds, int rS, int cS,
+                                    int D, float alpha) {
+  sx_impl<true>(out, S1, X1, S2, X2, lds, rS, cS, D, alpha);
+}
+template <typename OT>
+__device__ __forceinline__ void stx(OT* __restrict__ out, const float* S, int lds,
+                                    const float* X, int rS, int cS, int D, float alpha) {
+  stx_impl<false>(out, S, X, nullptr, nullptr, lds, rS, cS, D, alpha);
+}
+template <typename OT>
+__device__ __forceinline__ void stx2(OT* __restrict__ out, const float* S1, const float* X1,
+                                     const float* S2, const float* X2, int lds, int rS, int cS,
+                                     int D, float alpha) {
+  stx_impl<true>(out, S1, X1, S2, X2, lds, rS, cS, D, alpha);
+}
+
+__device__ __forceinline__ bool masked(int i, int j, int causal) { return causal && j > i; }
 
 // P[i][j] = exp(S[i][j] - lse_i) in place (0 where masked).
 __device__ __forceinline__ void probs_from_lse(float* S, int lds, const float* lse_s, int T,
