@@ -160,6 +160,34 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
+# ------------------------------------------------------------------ host placement
+def bind_to_gpu_numa(dev):
+    """Pin this process to the CPUs of the GPU's own NUMA node (read from
+    sysfs), so pinned host buffers allocated afterwards live next to the
+    GPU's PCIe root and host<->device copies do not cross sockets.  Returns
+    the CPU list used, or None when the topology is not available."""
+    try:
+        pr = torch.cuda.get_device_properties(dev)
+        bus = f"{pr.pci_domain_id:04x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+        path = f"/sys/bus/pci/devices/{bus}/local_cpulist"
+        if not os.path.exists(path):
+            return None
+        cpus = set()
+        for part in open(path).read().strip().split(","):
+            if "-" in part:
+                a, b = part.split("-")
+                cpus.update(range(int(a), int(b) + 1))
+            elif part:
+                cpus.add(int(part))
+        cpus &= os.sched_getaffinity(0)
+        if cpus:
+            os.sched_setaffinity(0, cpus)
+            return sorted(cpus)
+    except (OSError, ValueError, AttributeError):
+        return None
+    return None
+
+
 # ------------------------------------------------------------------ helpers
 def randn(shape, gen, dtype, device):
     return torch.randn(*shape, generator=gen, dtype=torch.float32).to(dtype).to(device)
@@ -457,6 +485,8 @@ def theria_arm(args, world, rank, local):
     from theria_b200 import _lib
     _lib.load()
     dev = torch.device("cuda", local)
+    all_cpus = os.sched_getaffinity(0)
+    numa_cpus = bind_to_gpu_numa(dev)
     peaks, peak_src = load_peaks()
     causal = args.workload == "fwdbwd_causal"
     res = run_fwdbwd(args, world, rank, dev, causal=causal)
@@ -483,6 +513,7 @@ def theria_arm(args, world, rank, local):
                 "launch_ms": res["t_bwd_ms"],
                 "fwd": {"achieved": res["fwd_tflops"], "frac": res["fwd_tflops"] / peak,
                         "launch_ms": res["t_fwd_ms"]}}
+    os.sched_setaffinity(0, all_cpus)  # the CPU baseline uses every host core
     cores = cpu_threads()
     tf, units, secs = cpu_fwdbwd_sample(budget_s=args.cpu_budget)
     cfg = dict(CONFIG, global_batch=4 * world, parallelism=f"dp{world}")
@@ -493,7 +524,9 @@ def theria_arm(args, world, rank, local):
         "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": res["ms_per_step"], "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic N(0,1), seeded per rank",
-        "config": cfg, "e2e": res["e2e"], "gpu_launches": res["gpu_launches"],
+        "config": cfg, "e2e": dict(res["e2e"], host_cpus=(
+            f"{len(numa_cpus)} CPUs of the GPU's NUMA node" if numa_cpus else "unbound")),
+        "gpu_launches": res["gpu_launches"],
         "clocks": res["clocks"], "roofline": roofline,
         "cpu_baseline": {"value": tf, "unit": "TFLOP/s", "cores": cores, "kind": "port",
                          "sample": f"CPU oracle fwd+bwd, bf16, {units} (b,h) units "
