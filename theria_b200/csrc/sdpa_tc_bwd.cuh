@@ -18,8 +18,14 @@
 // double buffer [384 + 64b, 448 + 64b); for D = 64 as dQ = dS K for a PAIR of
 // query tiles at once (M = 128 query rows, the two adjacent dS^T buffers read
 // as one MN-major operand) into [256, 320).
-// Warp roles: warp 0 TMA, warp 1 MMA issuer + TMEM owner, warps 2..9 two
-// groups of four (one per TMEM lane quarter) splitting the columns.
+// Warp roles: warp 0 TMA; warp 1 issues S^T/dP^T and owns TMEM; warp 2
+// issues dV/dK/dQ; warps 3..10 two groups of four (one per TMEM lane quarter)
+// splitting the columns; warps 11..14 flush dQ.  Two issuing threads: one
+// thread issues a tcgen05.mma only every ~60 cycles, slower than the tensor
+// core runs the N = 64 products, and each barrier wait between groups stalls
+// its issue stream; with the two groups on separate threads each hides the
+// other's waits.  The groups touch disjoint TMEM columns, and every
+// cross-group dependency already passes through the compute warps' barriers.
 #pragma once
 
 #include "tc_common.cuh"
@@ -31,7 +37,8 @@ constexpr int BK = 128;        // keys per CTA (M of S^T, dP^T, dV, dK)
 constexpr int BQ = 64;         // query rows per iteration (N of S^T, dP^T)
 constexpr int NCOMPUTE = 256;  // 8 compute warps: 2 groups x 4 TMEM lane quarters
 constexpr int NDQ = 128;       // 4 warps that flush dQ (one per TMEM lane quarter)
-constexpr int NTHREADS = 64 + NCOMPUTE + NDQ;
+constexpr int NTHREADS = 96 + NCOMPUTE + NDQ;
+constexpr int kFirstCompute = 3;  // warps 0..2: TMA, S/dP issuer, dV/dK/dQ issuer
 
 template <int HD>
 struct Smem {
@@ -40,17 +47,19 @@ struct Smem {
   // Q/dO ring depth: a stage is released only when the tile's last MMAs
   // complete, so the ring must cover that latency plus the TMA refill.
   static constexpr int QST = HD == 128 ? 3 : 4;
-  static constexpr int kP = BK * BQ * 2;    // one P^T or dS^T buffer [key][q]
+  static constexpr int kP = BK * BQ * 2;    // one dS^T buffer [key][q]
+  // fp32 dQ tile [q][d] staged for the bulk reduction (D = 128 only)
+  static constexpr int kStage = HD == 128 ? BQ * HD * 4 : 0;
   static constexpr int oK = 0;
   static constexpr int oV = oK + kKV;
   static constexpr int oQ = oV + kKV;       // QST stages
   static constexpr int oDO = oQ + QST * kQ; // QST stages
-  static constexpr int oP = oDO + QST * kQ; // 2 buffers
-  static constexpr int oDS = oP + 2 * kP;   // 2 buffers (adjacent: a pair is one M=128 operand)
-  static constexpr int oBar = oDS + 2 * kP;
+  static constexpr int oDS = oDO + QST * kQ;  // 2 buffers (adjacent: a pair is one M=128 operand)
+  static constexpr int oStage = oDS + 2 * kP;
+  static constexpr int oBar = oStage + kStage;
   // kv_full, q_full[4], q_empty[4], s_full, s_read, p_full[2], mma2_done[2],
-  // dq_free[2], drain
-  static constexpr int nBar = 1 + 8 + 2 + 6 + 1;
+  // dq_free[2], drain[2], stage_free, stage_full
+  static constexpr int nBar = 1 + 8 + 2 + 6 + 2 + 2;
   static constexpr int oTmem = oBar + nBar * 8;
   static constexpr int oAbort = oTmem + 4;
   static constexpr int kBytes = oAbort + 4;
@@ -115,10 +124,12 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
   uint64_t* q_empty = bars + 5;     // [QST] stage free (MMAs reading it done)
   uint64_t* s_full = bars + 9;      // S^T, dP^T of the current tile computed
   uint64_t* s_read = bars + 10;     // ... and loaded by the compute warps (256 arrivals)
-  uint64_t* p_full = bars + 11;     // [2] P^T, dS^T of the buffer written (256 arrivals)
+  uint64_t* p_full = bars + 11;     // [2] P^T (TMEM), dS^T (smem) of buffer b written (256 arrivals)
   uint64_t* mma2_done = bars + 13;  // [2] dV, dK (and dQ) MMAs of the tile done
-  uint64_t* dq_free = bars + 15;    // [2] dQ of the buffer flushed (128 arrivals)
-  uint64_t* drain = bars + 17;
+  uint64_t* dq_free = bars + 15;    // dQ read out of TMEM (128 arrivals); [1] unused
+  uint64_t* drain = bars + 17;      // [2] each issuer's last MMAs done
+  uint64_t* stage_free = bars + 19; // dQ staging buffer read by the previous reduction
+  uint64_t* stage_full = bars + 20; // dQ staging buffer written (128 arrivals)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::oTmem);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + L::oAbort);
 
@@ -128,6 +139,7 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
   const int n_qt = (Tq + BQ - 1) / BQ;
   const int i_begin = CAUSAL ? k0 / BQ : 0;  // first query tile that sees these keys
   const int n_iter = n_qt > i_begin ? n_qt - i_begin : 0;
+  auto tile_of = [&](int t) { return i_begin + t; };
 
   if (threadIdx.x == 0) {
     tc::mbar_init(kv_full, 1);
@@ -143,6 +155,9 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
     tc::mbar_init(s_full, 1);
     tc::mbar_init(s_read, NCOMPUTE);
     tc::mbar_init(drain, 1);
+    tc::mbar_init(drain + 1, 1);
+    tc::mbar_init(stage_free, 1);
+    tc::mbar_init(stage_full, NDQ);
     *abort = 0;
     tc::fence_barrier_init();
   }
@@ -152,8 +167,10 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
   tc::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   // TMEM: S^T [0,64), dP^T [64,128), dV [128,128+D), dK [128+D,128+2D),
-  // dQ^T buffers [384+64b, 448+64b) (D=128) or the pair dQ [256,320) (D=64).
+  // dQ^T [384,448) (D=128) or the pair dQ [256,320) (D=64), and the packed
+  // 16-bit P^T buffers [448+32b, 480+32b).
   const uint32_t t_dv = tmem + 128, t_dk = tmem + 128 + HD, t_dqp = tmem + 256;
+  const uint32_t t_dqt = tmem + 384, t_pt = tmem + 448;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -169,7 +186,7 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       for (int t = 0; t < n_iter; ++t) {
         const int st = t % QST;
         if (t >= QST && !tc::mbar_wait(q_empty + st, ((t / QST) - 1) & 1, abort)) break;
-        const int q0 = (i_begin + t) * BQ;
+        const int q0 = tile_of(t) * BQ;
         tc::mbar_expect_tx(q_full + st, 2 * L::kQ);
         for (int cb = 0; cb < HD / 64; ++cb) {
           tc::tma_load_3d(smem + L::oQ + st * L::kQ + cb * BQ * 128, &tm_q, q_full + st,
@@ -183,8 +200,8 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       for (int t = issued > QST ? issued - QST : 0; t < issued; ++t)
         tc::mbar_wait_drain(q_full + t % QST, (t / QST) & 1);
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
+  } else if (warp == 1 || warp == 2) {
+    // ------------------------------------------------------------ MMA issuers
     if (lane == 0 && n_iter > 0) {
       constexpr int ab = tc::AbFmt<T>::v;
       constexpr uint32_t id_s = tc::idesc_f16(BK, BQ, ab, 0, 0);    // S^T, dP^T
@@ -193,79 +210,86 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       constexpr uint32_t id_dqp = tc::idesc_f16(2 * BQ, HD, ab, 1, 1);  // pair dQ (HD == 64)
       const uint32_t a_k = tc::smem_u32(smem + L::oK), a_v = tc::smem_u32(smem + L::oV);
       const uint32_t a_q = tc::smem_u32(smem + L::oQ), a_do = tc::smem_u32(smem + L::oDO);
-      const uint32_t a_p = tc::smem_u32(smem + L::oP), a_ds = tc::smem_u32(smem + L::oDS);
-      // base descriptors (K-major "k", MN-major "m"), advanced by constant adds
-      const uint64_t kK = tc::sw128_desc(a_k, 16, 1024), kV = tc::sw128_desc(a_v, 16, 1024);
-      const uint64_t kQ = tc::sw128_desc(a_q, 16, 1024), kDO = tc::sw128_desc(a_do, 16, 1024);
-      const uint64_t kP = tc::sw128_desc(a_p, 16, 1024), kDS = tc::sw128_desc(a_ds, 16, 1024);
-      const uint64_t mQ = tc::sw128_desc(a_q, BQ * 128, 1024);
-      const uint64_t mDO = tc::sw128_desc(a_do, BQ * 128, 1024);
-      const uint64_t mK = tc::sw128_desc(a_k, BK * 128, 1024);
-      const uint64_t mDS = tc::sw128_desc(a_ds, BK * 128, 1024);
-      const uint64_t mDSpair = tc::sw128_desc(a_ds, L::kP, 1024);
-      auto issue_s = [&](int t) -> bool {
-        const int st = t % QST;
-        if (!tc::mbar_wait(q_full + st, (t / QST) & 1, abort)) return false;
-        // the single S^T/dP^T buffer is free once the previous tile was loaded
-        if (t >= 1 && !tc::mbar_wait(s_read, (t - 1) & 1, abort)) return false;
-        tc::tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t off_a = (kk / 4) * (BK * 128) + (kk % 4) * 32;
-          const uint32_t off_b = st * L::kQ + (kk / 4) * (BQ * 128) + (kk % 4) * 32;
-          tc::mma_ss(tmem + 64, tc::desc_at(kV, off_a), tc::desc_at(kDO, off_b), id_s,
-                     kk > 0 ? 1u : 0u);
-          tc::mma_ss(tmem, tc::desc_at(kK, off_a), tc::desc_at(kQ, off_b), id_s,
-                     kk > 0 ? 1u : 0u);
-        }
-        tc::mma_commit(s_full);
-        return true;
-      };
+      const uint32_t a_ds = tc::smem_u32(smem + L::oDS);
       bool ok = tc::mbar_wait(kv_full, 0, abort);
-      if (ok) ok = issue_s(0);
-      for (int t = 0; ok && t < n_iter; ++t) {
-        const int b = t & 1;
-        if (t + 1 < n_iter && !issue_s(t + 1)) break;
-        if (!tc::mbar_wait(p_full + b, (t >> 1) & 1, abort)) break;
-        tc::tc_fence_after();
-        const uint32_t pbo = b * L::kP;  // this tile's P^T / dS^T buffer offset
-#pragma unroll
-        for (int kk = 0; kk < BQ / 16; ++kk) {
-          // contraction over the tile's queries: P^T / dS^T K-major, dO / Q MN-major
-          const uint32_t off_b = (t % QST) * L::kQ + kk * 16 * 128;
-          const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
-          tc::mma_ss(t_dv, tc::desc_at(kP, pbo + kk * 32), tc::desc_at(mDO, off_b), id_kv, acc);
-          tc::mma_ss(t_dk, tc::desc_at(kDS, pbo + kk * 32), tc::desc_at(mQ, off_b), id_kv, acc);
-        }
-        if constexpr (!kPairDq) {
-          // dQ^T = K^T dS^T over the keys, into dQ^T buffer b
-          if (t >= 2 && !tc::mbar_wait(dq_free + b, ((t - 2) >> 1) & 1, abort)) break;
+      if (warp == 1) {
+        // S^T = K Q_t^T and dP^T = V dO_t^T into the single S/dP buffer,
+        // which is free once the compute warps loaded the previous tile.
+        const uint64_t kK = tc::sw128_desc(a_k, 16, 1024), kV = tc::sw128_desc(a_v, 16, 1024);
+        const uint64_t kQ = tc::sw128_desc(a_q, 16, 1024), kDO = tc::sw128_desc(a_do, 16, 1024);
+        for (int t = 0; ok && t < n_iter; ++t) {
+          const int st = t % QST;
+          if (!tc::mbar_wait(q_full + st, (t / QST) & 1, abort)) break;
+          if (t >= 1 && !tc::mbar_wait(s_read, (t - 1) & 1, abort)) break;
           tc::tc_fence_after();
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk)
-            tc::mma_ss(tmem + 384 + b * 64, tc::desc_at(mK, kk * 2048),
-                       tc::desc_at(mDS, pbo + kk * 2048), id_dqt, kk > 0 ? 1u : 0u);
-        } else if ((t & 1) || t == n_iter - 1) {
-          // dQ for the pair (2p, 2p+1): both dS^T buffers as one M = 128 operand
-          const int p = t >> 1;
-          if (p > 0 && !tc::mbar_wait(dq_free, (p - 1) & 1, abort)) break;
-          tc::tc_fence_after();
-#pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk)
-            tc::mma_ss(t_dqp, tc::desc_at(mDSpair, kk * 2048), tc::desc_at(mK, kk * 2048),
-                       id_dqp, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < HD / 16; ++kk) {
+            const uint32_t off_a = (kk / 4) * (BK * 128) + (kk % 4) * 32;
+            const uint32_t off_b = st * L::kQ + (kk / 4) * (BQ * 128) + (kk % 4) * 32;
+            tc::mma_ss(tmem + 64, tc::desc_at(kV, off_a), tc::desc_at(kDO, off_b), id_s,
+                       kk > 0 ? 1u : 0u);
+            tc::mma_ss(tmem, tc::desc_at(kK, off_a), tc::desc_at(kQ, off_b), id_s,
+                       kk > 0 ? 1u : 0u);
+          }
+          tc::mma_commit(s_full);
         }
-        tc::mma_commit(mma2_done + b);
-        tc::mma_commit(q_empty + t % QST);
+        tc::mma_commit(drain);
+        tc::mbar_wait_drain(drain, 0);
+      } else {
+        // dV += P^T dO_t, dK += dS^T Q_t, then dQ; releases the Q/dO stage.
+        const uint64_t kDS = tc::sw128_desc(a_ds, 16, 1024);
+        const uint64_t mQ = tc::sw128_desc(a_q, BQ * 128, 1024);
+        const uint64_t mDO = tc::sw128_desc(a_do, BQ * 128, 1024);
+        const uint64_t mK = tc::sw128_desc(a_k, BK * 128, 1024);
+        const uint64_t mDS = tc::sw128_desc(a_ds, BK * 128, 1024);
+        const uint64_t mDSpair = tc::sw128_desc(a_ds, L::kP, 1024);
+        for (int t = 0; ok && t < n_iter; ++t) {
+          const int b = t & 1;
+          if (!tc::mbar_wait(p_full + b, (t >> 1) & 1, abort)) break;
+          tc::tc_fence_after();
+          const uint32_t pbo = b * L::kP;  // this tile's dS^T buffer offset
+#pragma unroll
+          for (int kk = 0; kk < BQ / 16; ++kk) {
+            // contraction over the tile's queries: P^T from TMEM (8 packed
+            // columns per 16 queries), dS^T K-major in smem, dO / Q MN-major
+            const uint32_t off_b = (t % QST) * L::kQ + kk * 16 * 128;
+            const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
+            tc::mma_ts(t_dv, t_pt + b * 32 + kk * 8, tc::desc_at(mDO, off_b), id_kv, acc);
+            tc::mma_ss(t_dk, tc::desc_at(kDS, pbo + kk * 32), tc::desc_at(mQ, off_b), id_kv,
+                       acc);
+          }
+          if constexpr (!kPairDq) {
+            // dQ^T = K^T dS^T over the keys, once the previous dQ^T was read
+            if (t >= 1 && !tc::mbar_wait(dq_free, (t - 1) & 1, abort)) break;
+            tc::tc_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < BK / 16; ++kk)
+              tc::mma_ss(t_dqt, tc::desc_at(mK, kk * 2048),
+                         tc::desc_at(mDS, pbo + kk * 2048), id_dqt, kk > 0 ? 1u : 0u);
+          } else if ((t & 1) || t == n_iter - 1) {
+            // dQ for the pair (2p, 2p+1): both dS^T buffers as one M = 128 operand
+            const int p = t >> 1;
+            if (p > 0 && !tc::mbar_wait(dq_free, (p - 1) & 1, abort)) break;
+            tc::tc_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < BK / 16; ++kk)
+              tc::mma_ss(t_dqp, tc::desc_at(mDSpair, kk * 2048), tc::desc_at(mK, kk * 2048),
+                         id_dqp, kk > 0 ? 1u : 0u);
+          }
+          tc::mma_commit(mma2_done + b);
+          // S^T/dP^T of tile t also read this stage; they completed before
+          // the compute warps could publish p_full for tile t.
+          tc::mma_commit(q_empty + t % QST);
+        }
+        tc::mma_commit(drain + 1);
+        tc::mbar_wait_drain(drain + 1, 0);
       }
-      tc::mma_commit(drain);
-      tc::mbar_wait_drain(drain, 0);
     }
-  } else if (warp < 2 + NCOMPUTE / 32) {
+  } else if (warp < kFirstCompute + NCOMPUTE / 32) {
     // ------------------------------------------------------------ compute
-    // Warps 2..9: P^T and dS^T, then dK / dV at the end.  Group `grp`
+    // Warps 3..10: P^T and dS^T, then dK / dV at the end.  Group `grp`
     // handles query columns [32 grp, 32 grp + 32) of each tile.
-    const int grp = (warp - 2) >> 2;
+    const int grp = (warp - kFirstCompute) >> 2;
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;  // TMEM lane = key row
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
@@ -274,11 +298,11 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
     auto wait = [&](uint64_t* bar, uint32_t parity) {
       return __all_sync(0xffffffffu, tc::mbar_wait(bar, parity, abort));
     };
-    const uint32_t a_p = tc::smem_u32(smem + L::oP), a_ds = tc::smem_u32(smem + L::oDS);
+    const uint32_t a_ds = tc::smem_u32(smem + L::oDS);
     const size_t row_base = (size_t)bh * Tq;
     for (int t = 0; t < n_iter; ++t) {
       const int b = t & 1;
-      const int q0 = (i_begin + t) * BQ;
+      const int q0 = tile_of(t) * BQ;
       // Row statistics of this group's 32 queries: one load per lane, then
       // broadcast by shuffles.
       const int ql = q0 + grp * 32 + lane;
@@ -291,7 +315,7 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       tc::tmem_ld32(tmem + 64 + lane_off + grp * 32, dp);
       tc::tc_fence_before();
       tc::mbar_arrive(s_read);  // the tensor core may start on the next tile
-      // P^T / dS^T buffer b is free once the MMAs that read it are done:
+      // P^T / dS^T buffers b are free once the MMAs that read them are done:
       // tile t-2's dV/dK (and dQ); with paired dQ, an even tile's buffer is
       // also read by the pair MMA issued with tile t-1.
       if (t >= 2) {
@@ -313,17 +337,21 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
         s[e] = p;                   // P^T
         dp[e] = p * (dp[e] - zq);   // dS^T
       }
-      const uint32_t pb = a_p + b * L::kP, db = a_ds + b * L::kP;
+      // P^T stays in TMEM as packed 16-bit pairs (A operand of dV += P^T dO);
+      // dS^T goes to shared memory (operand of dK and dQ).
+      uint32_t pk[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) pk[i] = tc::pack2<T>(s[2 * i], s[2 * i + 1]);
+      tc::tmem_st16(t_pt + b * 32 + grp * 16 + lane_off, pk);
+      const uint32_t db = a_ds + b * L::kP;
 #pragma unroll
       for (int h = 0; h < 4; ++h) {
         const uint32_t off = tc::sw128_off(r, grp * 4 + h);
-        const float* pe = s + h * 8;
         const float* de = dp + h * 8;
-        tc::st_shared_v4(pb + off, tc::pack2<T>(pe[0], pe[1]), tc::pack2<T>(pe[2], pe[3]),
-                         tc::pack2<T>(pe[4], pe[5]), tc::pack2<T>(pe[6], pe[7]));
         tc::st_shared_v4(db + off, tc::pack2<T>(de[0], de[1]), tc::pack2<T>(de[2], de[3]),
                          tc::pack2<T>(de[4], de[5]), tc::pack2<T>(de[6], de[7]));
       }
+      tc::tmem_wait_st();
       tc::fence_proxy_async_smem();
       tc::tc_fence_before();
       tc::mbar_arrive(p_full + b);
@@ -367,12 +395,13 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
     }
   } else {
     // ------------------------------------------------------------ dQ flush
-    // Warps 10..13: read each finished dQ out of TMEM and add it (scaled)
+    // Warps 11..14: read each finished dQ out of TMEM and add it (scaled)
     // into the fp32 accumulator, concurrently with the next tile's compute.
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const size_t row_base = (size_t)bh * Tq;
+    const bool bulk_issuer = warp == kFirstCompute + NCOMPUTE / 32 && lane == 0;
     auto wait = [&](uint64_t* bar, uint32_t parity) {
       return __all_sync(0xffffffffu, tc::mbar_wait(bar, parity, abort));
     };
@@ -381,23 +410,41 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       if (!wait(mma2_done + (t & 1), (t >> 1) & 1)) break;
       tc::tc_fence_after();
       if constexpr (!kPairDq) {
-        // dQ^T of tile t: lane = head-dim index r, 64 query columns
-        const int qb = (i_begin + t) * BQ;
-#pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
-          float v[32];
-          tc::tmem_ld32(tmem + 384 + (t & 1) * 64 + lane_off + c * 32, v);
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int q = qb + c * 32 + e;
-            if (q < Tq) atomicAdd(dq_acc + (row_base + q) * HD + r, v[e] * scale);
-          }
-        }
+        // dQ^T of tile t (lane = head-dim index r, 64 query columns): read
+        // it out of TMEM, release the buffer, stage it scaled as fp32 rows
+        // [q][d] and add the tile to dQacc with one bulk reduction.  The
+        // staging buffer is reused once the previous reduction has read it.
+        const int qb = tile_of(t) * BQ;
+        float v0[32], v1[32];
+        tc::tmem_ld32(t_dqt + lane_off, v0);
+        tc::tmem_ld32(t_dqt + lane_off + 32, v1);
         tc::tc_fence_before();
-        tc::mbar_arrive(dq_free + (t & 1));
+        tc::mbar_arrive(dq_free);
+        if (bulk_issuer) {
+          tc::bulk_wait_read_all();
+          tc::mbar_arrive(stage_free);
+        }
+        if (!wait(stage_free, t & 1)) break;
+        float* stage = reinterpret_cast<float*>(smem + L::oStage);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          stage[e * HD + r] = v0[e] * scale;
+          stage[(32 + e) * HD + r] = v1[e] * scale;
+        }
+        tc::fence_proxy_async_smem();
+        tc::mbar_arrive(stage_full);
+        bool staged = true;
+        if (bulk_issuer) {
+          staged = tc::mbar_wait(stage_full, t & 1, abort);
+          const int rows = Tq - qb < BQ ? Tq - qb : BQ;
+          if (staged)
+            tc::bulk_reduce_add_f32(dq_acc + (row_base + qb) * HD, smem + L::oStage,
+                                    (uint32_t)(rows * HD * 4));
+        }
+        if (!__shfl_sync(0xffffffffu, staged, 0)) break;
       } else {
         // dQ of the pair ending at tile t: lane = query row, 64 head dims
-        const int q = (i_begin + (t & ~1)) * BQ + r;
+        const int q = tile_of(t & ~1) * BQ + r;
 #pragma unroll 1
         for (int c = 0; c < 2; ++c) {
           float v[32];
@@ -414,6 +461,9 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
         tc::mbar_arrive(dq_free);
       }
     }
+    // the last reductions must finish before the CTA (and its staging
+    // buffer) goes away
+    if (bulk_issuer) tc::bulk_wait_all();
   }
   // ------------------------------------------------------------ teardown
   tc::tc_fence_before();

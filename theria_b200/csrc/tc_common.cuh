@@ -100,6 +100,25 @@ __device__ __forceinline__ void named_bar(uint32_t id, uint32_t count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
+// ---------------------------------------------------------------- bulk reduce
+// dst[0 .. bytes/4) += src[0 .. bytes/4) (fp32, in L2) by the TMA unit, as one
+// bulk-async group.  dst and src 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_reduce_add_f32(float* dst, const void* src, uint32_t bytes) {
+  asm volatile(
+      "cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f32 [%0], [%1], %2;\n\t"
+      "cp.async.bulk.commit_group;" ::"l"(dst),
+      "r"(smem_u32(src)), "r"(bytes)
+      : "memory");
+}
+// Wait until every bulk group of this thread has finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Wait until every bulk group of this thread has completed.
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- TMA
 // 3-D tiled load of box {64 elems, rows, 1} at (x, y, z) into smem,
 // completing on `bar` (transaction bytes).  x must be 16-byte aligned in
