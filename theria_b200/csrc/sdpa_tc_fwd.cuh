@@ -9,8 +9,9 @@
 // TMEM (512 columns): S_t at [128t, 128t+128) and O_t at [256 + t*D, ...).
 // The tensor core alternates between the tiles (S_0, S_1, PV_0, PV_1, ...)
 // so that one tile's softmax runs while the other tile's MMAs do.
-// Softmax reads S in two passes (row max, then exponentials) so a thread
-// holds 32 scores at a time, and writes P as packed 16-bit pairs over the
+// Softmax reads a thread's whole row of S with one TMEM load (128 registers),
+// takes the row max and the exponentials from registers, and writes P as
+// packed 16-bit pairs over the
 // first 64 columns of its own S; the PV MMA then takes P straight from TMEM
 // as its A operand (no shared-memory round trip).  In-order completion of
 // one thread's tcgen05 operations makes this safe: S_t(j+1) is issued after
@@ -41,9 +42,9 @@ struct Smem {
   static constexpr int oK = oQ + NQT * kQ;
   static constexpr int oV = oK + STAGES * kKV;
   static constexpr int oBar = oV + STAGES * kKV;
-  // q_full, k_full[S], v_full[S], kv_empty[S], s_full[2], p_full[2],
-  // o_done[2], drain
-  static constexpr int nBar = 1 + 3 * STAGES + 6 + 1;
+  // q_full, k_full[S], v_full[S], k_empty[S], v_empty[S], s_full[2],
+  // p_full[2], o_done[2], drain
+  static constexpr int nBar = 1 + 4 * STAGES + 6 + 1;
   static constexpr int oTmem = oBar + nBar * 8;
   static constexpr int oAbort = oTmem + 4;
   static constexpr int kBytes = oAbort + 4;
@@ -63,8 +64,11 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
   uint64_t* v_full = k_full + STAGES;
-  uint64_t* kv_empty = v_full + STAGES;
-  uint64_t* s_full = kv_empty + STAGES;  // [2] per query tile
+  // K and V stages are released separately: K_j once both S_t(j) are done
+  // (a step before V_j, which PV_t(j) reads), so the next K load starts early.
+  uint64_t* k_empty = v_full + STAGES;
+  uint64_t* v_empty = k_empty + STAGES;
+  uint64_t* s_full = v_empty + STAGES;  // [2] per query tile
   uint64_t* p_full = s_full + 2;         // [2]
   uint64_t* o_done = p_full + 2;         // [2]
   uint64_t* drain = o_done + 2;
@@ -83,7 +87,8 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
     for (int s = 0; s < STAGES; ++s) {
       tc::mbar_init(k_full + s, 1);
       tc::mbar_init(v_full + s, 1);
-      tc::mbar_init(kv_empty + s, 1);
+      tc::mbar_init(k_empty + s, 1);
+      tc::mbar_init(v_empty + s, 1);
     }
     for (int t = 0; t < 2; ++t) {
       tc::mbar_init(s_full + t, 1);
@@ -114,11 +119,16 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
                           q0 + t * BM, bh);
       for (int j = 0; j < n_tiles; ++j) {
         const int st = j % STAGES;
-        if (j >= STAGES && !tc::mbar_wait(kv_empty + st, ((j / STAGES) - 1) & 1, abort)) break;
+        if (j >= STAGES && !tc::mbar_wait(k_empty + st, ((j / STAGES) - 1) & 1, abort)) break;
         tc::mbar_expect_tx(k_full + st, L::kKV);
         for (int cb = 0; cb < HD / 64; ++cb)
           tc::tma_load_3d(smem + L::oK + st * L::kKV + cb * BN * 128, &tm_k, k_full + st,
                           cb * 64, j * BN, bh);
+        if (j >= STAGES && !tc::mbar_wait(v_empty + st, ((j / STAGES) - 1) & 1, abort)) {
+          issued = j;  // K_j was issued; the drain below waits for it separately
+          tc::mbar_wait_drain(k_full + st, (j / STAGES) & 1);
+          break;
+        }
         tc::mbar_expect_tx(v_full + st, L::kKV);
         for (int cb = 0; cb < HD / 64; ++cb)
           tc::tma_load_3d(smem + L::oV + st * L::kKV + cb * BN * 128, &tm_v, v_full + st,
@@ -152,6 +162,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
                      tc::desc_at(dk, (kk / 4) * (BN * 128) + (kk % 4) * 32), id_s,
                      kk > 0 ? 1u : 0u);
         tc::mma_commit(s_full + t);
+        if (t == NQT - 1) tc::mma_commit(k_empty + j % STAGES);
       };
       bool ok = tc::mbar_wait(q_full, 0, abort) && tc::mbar_wait(k_full, 0, abort);
       if (ok) {
@@ -173,7 +184,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
             tc::mma_ts(tmem + 256 + t * HD, tmem + t * 128 + kk * 8, tc::desc_at(dv, kk * 2048),
                        id_pv, (j > 0 || kk > 0) ? 1u : 0u);
           if (!more) tc::mma_commit(o_done + t);
-          if (t == NQT - 1) tc::mma_commit(kv_empty + st);
+          if (t == NQT - 1) tc::mma_commit(v_empty + st);
           if (more) {
             if (t == 0) {
               if (!tc::mbar_wait(k_full + (j + 1) % STAGES, ((j + 1) / STAGES) & 1, abort)) {
@@ -213,23 +224,20 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       // tile) take a separate, slower path; the test is uniform per tile.
       const bool edge = (col0 + BN > M) || (CAUSAL && col0 + BN - 1 > q0 + t * BM);
       const int lim = CAUSAL ? min(M, row + 1) - col0 : M - col0;  // valid columns < lim
-      // pass 1: row maximum (64-column TMEM loads; 8 independent partial
-      // maxima so the reduction is not one 128-long dependent chain)
+      // The whole row of S comes out of TMEM in one load (one wait on the
+      // load latency per tile); the maximum uses 8 independent partial
+      // maxima so the reduction is not one 128-long dependent chain.
+      float v[BN];
+      tc::tmem_ld128(t_s, v);
       float mp[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) mp[i] = -INFINITY;
+      if (!edge) {
 #pragma unroll
-      for (int c = 0; c < BN / 64; ++c) {
-        float v[64];
-        tc::tmem_ld64(t_s + c * 64, v);
-        if (!edge) {
+        for (int i = 0; i < BN; ++i) mp[i & 7] = fmaxf(mp[i & 7], v[i]);
+      } else {
 #pragma unroll
-          for (int i = 0; i < 64; ++i) mp[i & 7] = fmaxf(mp[i & 7], v[i]);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 64; ++i)
-            mp[i & 7] = fmaxf(mp[i & 7], c * 64 + i < lim ? v[i] : -INFINITY);
-        }
+        for (int i = 0; i < BN; ++i) mp[i & 7] = fmaxf(mp[i & 7], i < lim ? v[i] : -INFINITY);
       }
       float mt = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
                        fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
@@ -249,34 +257,32 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
         l *= alpha;
 #pragma unroll 1
         for (int c = 0; c < HD / 32; ++c) {
-          float v[32];
-          tc::tmem_ld32(t_o + c * 32, v);
+          float o[32];
+          tc::tmem_ld32(t_o + c * 32, o);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] *= alpha;
-          tc::tmem_st32(t_o + c * 32, v);
+          for (int i = 0; i < 32; ++i) o[i] *= alpha;
+          tc::tmem_st32(t_o + c * 32, o);
         }
       }
       m = m_use;
       const float m_sub = (m_use == -INFINITY) ? 0.f : m_use;
-      // pass 2: P = exp2(s - m), written as packed pairs over S's first 64 columns
+      // P = exp2(s - m), written as packed pairs over S's first 64 columns
       float rs[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // partial row sums
 #pragma unroll
       for (int c = 0; c < BN / 64; ++c) {
-        float v[64];
-        tc::tmem_ld64(t_s + c * 64, v);
         if (!edge) {
 #pragma unroll
-          for (int i = 0; i < 64; ++i) v[i] = tc::ex2(fmaf(v[i], scale_log2, -m_sub));
+          for (int i = 0; i < 64; ++i) v[c * 64 + i] = tc::ex2(fmaf(v[c * 64 + i], scale_log2, -m_sub));
         } else {
 #pragma unroll
           for (int i = 0; i < 64; ++i)
-            v[i] = c * 64 + i < lim ? tc::ex2(fmaf(v[i], scale_log2, -m_sub)) : 0.f;
+            v[c * 64 + i] = c * 64 + i < lim ? tc::ex2(fmaf(v[c * 64 + i], scale_log2, -m_sub)) : 0.f;
         }
         uint32_t pk[32];
 #pragma unroll
         for (int i = 0; i < 64; i += 2) {
-          rs[(i / 2) & 7] += v[i] + v[i + 1];
-          pk[i / 2] = tc::pack2<T>(v[i], v[i + 1]);
+          rs[(i / 2) & 7] += v[c * 64 + i] + v[c * 64 + i + 1];
+          pk[i / 2] = tc::pack2<T>(v[c * 64 + i], v[c * 64 + i + 1]);
         }
         tc::tmem_st32u(t_s + c * 32, pk);
       }
