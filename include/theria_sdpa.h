@@ -148,6 +148,28 @@ int theria_sdpa_bwd_noalloc(const void* q, const void* k, const void* v,
                             int64_t B, int64_t H, int64_t T, int64_t M, int64_t D,
                             int dtype, float scale, int causal, void* stream);
 
+/*
+ * Dense attention scores: out[b,h,t,m] = scale * sum_d q[b,h,t,d] k[b,h,m,d],
+ * out [B,H,T,M] row-major in out_dtype (THERIA_F32, or the input dtype).
+ * Replaces the reference's QK^T kernels theria/attention/triton_qk.py:16-70
+ * (_qk_kernel, fp32 out; callers pass scale 1) and triton_qk.py:394-455
+ * (_qk_kernel_fast, input-dtype out).  Accumulates in fp32.
+ */
+int theria_sdpa_scores(const void* q, const void* k, void* out, int out_dtype,
+                       int64_t B, int64_t H, int64_t T, int64_t M, int64_t D,
+                       int dtype, float scale, void* stream);
+
+/*
+ * Dense attention probabilities: out[b,h,t,m] = exp(scale * q_t . k_m -
+ * lse[b,h,t]) as fp32 [B,H,T,M] (zero for m > t when causal), where lse is
+ * the row log-sum-exp theria_sdpa_fwd wrote for the same q, k, scale.
+ * Replaces the fused QK^T + softmax kernel theria/attention/triton_qk.py:
+ * 130-240 (_qk_softmax_kernel, triton_qk_softmax).
+ */
+int theria_sdpa_probs(const void* q, const void* k, const float* lse, float* out,
+                      int64_t B, int64_t H, int64_t T, int64_t M, int64_t D,
+                      int dtype, float scale, int causal, void* stream);
+
 /* Number of kernels this library has launched in this process (all devices,
  * all threads); for accounting in benchmarks and tests. */
 int64_t theria_launch_count(void);

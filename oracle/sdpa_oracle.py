@@ -62,6 +62,13 @@ def attention(q, k, v, scale=None, causal=False):
     return torch.matmul(torch.softmax(s, dim=-1), v)
 
 
+def probs(q, k, scale=None, causal=False):
+    """P = softmax(scale q k^T) in fp64 (the probabilities of
+    ``theria/attention/reference_attention.py:9-19``, and what
+    ``theria/attention/triton_qk.py:130-190`` writes)."""
+    return torch.softmax(_scores(q.double(), k.double(), _scale(q, scale), causal), dim=-1)
+
+
 def row_stats(q, k, scale=None, causal=False):
     """Row max ``m`` and sum-exp ``l`` of the scaled scores, and LSE = m + log l.
 

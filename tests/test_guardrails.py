@@ -42,9 +42,23 @@ def test_forward_requires_cuda():
 
 def test_unknown_backend_is_rejected_not_rerouted():
     q, k, v = _cpu()
-    for name in ("reference", "triton_qk", "triton_fast", "bogus"):
+    for name in ("bogus", "triton_qk_fused", ""):
         with pytest.raises(ValueError, match="Unsupported sdpa_custom backend"):
             sdpa_custom(q, k, v, backend=name)
+
+
+def test_partial_kernel_backends_require_cuda():
+    # reference triton_qk.py:80, 193-194: the partial kernels assert CUDA
+    q, k, v = _cpu()
+    for name in ("triton_qk", "triton_ref", "triton", "triton_fast", "triton_qk_softmax"):
+        with pytest.raises(AssertionError):
+            sdpa_custom(q, k, v, backend=name)
+
+
+def test_causal_needs_a_fused_backend():
+    q, k, v = _cpu()
+    with pytest.raises(ValueError, match="causal"):
+        sdpa_custom(q, k, v, backend="triton_qk", causal=True)
 
 
 def test_no_cpu_fallback_for_fused_backend():

@@ -45,6 +45,8 @@ SIGNATURES = {
     "theria_sdpa_jvp": (_i, [_vp] * 8 + [_i64] * 5 + [_i, _f, _i, _vp]),
     "theria_sdpa_hvp": (_i, [_vp] * 12 + [_vp, _i64] + [_i64] * 5 + [_i, _f, _i, _vp]),
     "theria_sdpa_bwd_noalloc": (_i, [_vp] * 10 + [_i64] * 5 + [_i, _f, _i, _vp]),
+    "theria_sdpa_scores": (_i, [_vp, _vp, _vp, _i] + [_i64] * 5 + [_i, _f, _vp]),
+    "theria_sdpa_probs": (_i, [_vp] * 4 + [_i64] * 5 + [_i, _f, _i, _vp]),
     "theria_launch_count": (_i64, []),
     "theria_get_device_error": (_i, [ctypes.POINTER(ctypes.c_int), _vp]),
     "theria_clear_device_error": (_i, [_vp]),

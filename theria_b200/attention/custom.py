@@ -1,33 +1,68 @@
 """Public SDPA entry point with the reference's names.
 
-Mirrors ``theria/attention/custom.py:15-71``.  The reference's
-``backend=`` switch selected among CPU reference math and several Triton
-kernels; this library has one implementation (the sm_100a kernels), so the
-switch keeps only the names that denoted the fused, higher-order-capable
-operator and rejects the rest loudly instead of falling back.
+Mirrors ``theria/attention/custom.py:15-71``.  The ``backend=`` switch keeps
+the reference's names:
+
+* ``triton_full_fused`` (default here), ``triton_full_fused_phase8``,
+  ``fused``: the fused sm_100a operator (twice differentiable, forward-mode
+  capable);
+* ``custom``: ``SDPACustom`` (the same kernels behind the reference's
+  Function contract with explicit ``hvp`` / ``jvp``);
+* ``triton_qk`` / ``triton_ref`` / ``triton``, ``triton_fast``: scores from
+  the dense score kernel, then PyTorch softmax and PV, as the reference did;
+* ``triton_qk_softmax``: probabilities from the dense probability kernel,
+  then PyTorch PV;
+* ``reference``: the reference's formula softmax(q k^T / sqrt(D)) v in
+  PyTorch operations on the inputs' device (the comparison arm of the
+  reference's own tests, not a fallback: it runs only when asked for).
+
+Unknown names raise ``ValueError`` like the reference.
 """
 
 from __future__ import annotations
 
+import torch
+
 from theria_b200.attention.fused import SDPAFunction
+from theria_b200.attention.triton_qk import triton_qk, triton_qk_fast, triton_qk_softmax
 from theria_b200.autograd.sdpa_custom_function import SDPACustom
 
 FUSED_BACKENDS = ("triton_full_fused", "triton_full_fused_phase8", "custom", "fused")
+PARTIAL_BACKENDS = ("triton_qk", "triton_ref", "triton", "triton_fast", "triton_qk_softmax")
+BACKENDS = FUSED_BACKENDS + PARTIAL_BACKENDS + ("reference",)
+
+
+def _reference_formula(q, k, v):
+    # reference_attention.py:9-19: softmax(q k^T / sqrt(D)) v
+    scores = torch.matmul(q, k.transpose(-2, -1)) / (q.shape[-1] ** 0.5)
+    return torch.matmul(torch.softmax(scores, dim=-1), v)
 
 
 def sdpa_custom(q, k, v, *, backend: str = "triton_full_fused", causal: bool = False):
-    """softmax(q k^T / sqrt(D)) v on the CUDA kernels, returning q.dtype.
+    """softmax(q k^T / sqrt(D)) v, returning q.dtype.
 
-    Twice differentiable (``create_graph=True`` keeps the attention's own
-    curvature).  ``causal=True`` applies a top-left-aligned causal mask.
+    The fused backends are twice differentiable (``create_graph=True`` keeps
+    the attention's own curvature); ``causal=True`` (top-left aligned mask)
+    is available on the fused backends.
     """
-    if backend not in FUSED_BACKENDS:
-        raise ValueError(
-            f"Unsupported sdpa_custom backend: {backend} (theria_b200 provides only the "
-            f"fused CUDA operator: {', '.join(FUSED_BACKENDS)})")
+    if backend not in BACKENDS:
+        raise ValueError(f"Unsupported sdpa_custom backend: {backend}")
+    if causal and backend not in FUSED_BACKENDS:
+        raise ValueError(f"causal=True needs a fused backend ({', '.join(FUSED_BACKENDS)})")
     if backend == "custom":
         return SDPACustom.apply(q, k, v, causal)
-    return SDPAFunction.apply(q, k, v, causal, None)
+    if backend in FUSED_BACKENDS:
+        return SDPAFunction.apply(q, k, v, causal, None)
+    if backend == "reference":
+        return _reference_formula(q, k, v)
+    if backend == "triton_qk_softmax":
+        probs = triton_qk_softmax(q, k).to(torch.float32)
+        return torch.matmul(probs, v.to(probs.dtype)).to(q.dtype)
+    # custom.py:30-43: scores from the kernel, PyTorch softmax and PV
+    qk = triton_qk_fast if backend == "triton_fast" else triton_qk
+    scores = qk(q, k).to(torch.float32) / (q.shape[-1] ** 0.5)
+    probs = torch.softmax(scores, dim=-1)
+    return torch.matmul(probs, v.to(probs.dtype)).to(q.dtype)
 
 
 def sdpa_custom_hvp(q, k, v, dq, dk, dv):

@@ -92,6 +92,58 @@ def forward(q, k, v, *, causal=False, scale=None, out_dtype=None, need_lse=True)
     return o, lse
 
 
+def check_qk(q, k, what):
+    """Contract of the dense score / probability kernels (q and k only)."""
+    for name, t in (("q", q), ("k", k)):
+        _check_tensor(name, t, what)
+    if q.ndim != 4 or k.ndim != 4:
+        raise AssertionError("q and k must have shape (B,H,T,D) and (B,H,M,D)")
+    B, H, T, D = q.shape
+    if k.shape[0] != B or k.shape[1] != H or k.shape[3] != D:
+        raise AssertionError("Q and K last dimensions must match")
+    if k.dtype != q.dtype or k.device != q.device:
+        raise AssertionError("q and k must share one dtype and device")
+    if D > MAX_HEAD_DIM:
+        raise AssertionError(f"theria_b200 supports D<={MAX_HEAD_DIM}")
+    return B, H, T, k.shape[2], D
+
+
+def scores(q, k, *, scale=1.0, out_dtype=torch.float32):
+    """Dense S = scale q k^T as [B, H, T, M] (fp32 accumulation)."""
+    B, H, T, M, D = check_qk(q, k, "theria scores")
+    if out_dtype not in (torch.float32, q.dtype):
+        raise AssertionError("out_dtype must be float32 or q.dtype")
+    out = torch.empty((B, H, T, M), device=q.device, dtype=out_dtype)
+    lib = _lib.load()
+    with torch.cuda.device(q.device):
+        st = lib.theria_sdpa_scores(
+            _lib.ptr(q), _lib.ptr(k), _lib.ptr(out), _lib.DTYPE_CODE[out_dtype], B, H, T, M, D,
+            _lib.DTYPE_CODE[q.dtype], float(scale), _lib.stream_of(q))
+    _lib.check(st, "theria_sdpa_scores")
+    return out
+
+
+def probs(q, k, *, causal=False, scale=None, lse=None):
+    """Dense P = softmax(scale q k^T) as float32 [B, H, T, M].
+
+    The row logsumexp comes from the forward kernel (run with k as values
+    when ``lse`` is not given); the probabilities are then one tile pass.
+    """
+    B, H, T, M, D = check_qk(q, k, "theria probs")
+    scale = default_scale(q) if scale is None else float(scale)
+    if lse is None:
+        _, lse = forward(q, k, k, causal=causal, scale=scale)
+    _check_lse(lse, B, H, T)
+    out = torch.empty((B, H, T, M), device=q.device, dtype=torch.float32)
+    lib = _lib.load()
+    with torch.cuda.device(q.device):
+        st = lib.theria_sdpa_probs(
+            _lib.ptr(q), _lib.ptr(k), _lib.ptr(lse), _lib.ptr(out), B, H, T, M, D,
+            _lib.DTYPE_CODE[q.dtype], scale, int(bool(causal)), _lib.stream_of(q))
+    _lib.check(st, "theria_sdpa_probs")
+    return out
+
+
 def backward(q, k, v, dout, lse, *, o=None, causal=False, scale=None,
              need=(True, True, True)):
     """dQ, dK, dV of <O, dout>; entries of ``need`` that are False return None."""

@@ -10,6 +10,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "sdpa_scores.cuh"
 #include "sdpa_simt.cuh"
 #include "sdpa_small.cuh"
 #include "sdpa_tc_bwd.cuh"
@@ -421,6 +422,53 @@ bool use_tc(int dtype, const Shape& s, std::initializer_list<const void*> ptrs) 
   return true;
 }
 
+// Dense scores / probabilities (sdpa_scores.cuh).  Output element type O is
+// float, or T itself for 16-bit scores.
+template <typename T, typename O>
+int scores_launch(const void* q, const void* k, void* out, const float* lse, const Shape& s,
+                  int dtype, int mode, cudaStream_t st) {
+  const int vec = tc::aligned16(out) && (s.M * (int64_t)sizeof(O)) % 16 == 0;
+  if constexpr (!std::is_same<T, float>::value) {
+    if (use_tc(dtype, s, {q, k})) {
+      CUtensorMap mq, mk;
+      const int64_t bh = s.B * s.H;
+      if (tc::make_map_3d(&mq, q, dtype, bh, s.T, s.D, scores::TM) &&
+          tc::make_map_3d(&mk, k, dtype, bh, s.M, s.D, scores::TN)) {
+        dim3 grid((unsigned)((s.T + scores::TM - 1) / scores::TM),
+                  (unsigned)((s.M + scores::TN - 1) / scores::TN), (unsigned)bh);
+        if (s.D == 64) {
+          auto kern = scores::tc_kernel<T, O, 64>;
+          constexpr int smem = scores::TcSmem<64>::kAlloc;
+          cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+          kern<<<grid, 128, smem, st>>>(mq, mk, (O*)out, lse, (int)s.T, (int)s.M, s.scale, mode,
+                                        s.causal, vec);
+        } else {
+          auto kern = scores::tc_kernel<T, O, 128>;
+          constexpr int smem = scores::TcSmem<128>::kAlloc;
+          cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+          kern<<<grid, 128, smem, st>>>(mq, mk, (O*)out, lse, (int)s.T, (int)s.M, s.scale, mode,
+                                        s.causal, vec);
+        }
+        return launch_status();
+      }
+    }
+  }
+  dim3 grid((unsigned)((s.M + scores::ST - 1) / scores::ST),
+            (unsigned)((s.T + scores::ST - 1) / scores::ST), (unsigned)(s.B * s.H));
+  if (grid.y > 65535) return THERIA_ERR_UNSUPPORTED;
+  scores::simt_kernel<T, O><<<grid, dim3(16, 16), 0, st>>>(
+      (const T*)q, (const T*)k, (O*)out, lse, (int)s.T, (int)s.M, (int)s.D, s.scale, mode,
+      s.causal);
+  return launch_status();
+}
+
+template <typename T>
+int scores_dispatch(const void* q, const void* k, void* out, int out_dtype, const float* lse,
+                    const Shape& s, int dtype, int mode, cudaStream_t st) {
+  if (out_dtype == THERIA_F32) return scores_launch<T, float>(q, k, out, lse, s, dtype, mode, st);
+  return scores_launch<T, T>(q, k, out, lse, s, dtype, mode, st);
+}
+
 #define THERIA_DISPATCH(dtype, FN, ...)                          \
   ((dtype) == THERIA_F32   ? FN<float>(__VA_ARGS__)              \
    : (dtype) == THERIA_F16 ? FN<__half>(__VA_ARGS__)             \
@@ -468,6 +516,29 @@ int theria_sdpa_fwd(const void* q, const void* k, const void* v, void* o, int o_
     if (e >= 0) return e;
   }
   return THERIA_DISPATCH(dtype, simt_fwd, q, k, v, o, o_dtype, lse, s, st);
+}
+
+int theria_sdpa_scores(const void* q, const void* k, void* out, int out_dtype, int64_t B,
+                       int64_t H, int64_t T, int64_t M, int64_t D, int dtype, float scale,
+                       void* stream) {
+  if (int e = check_shape(B, H, T, M, D, dtype)) return e;
+  if (out_dtype != THERIA_F32 && out_dtype != dtype) return THERIA_ERR_INVALID_ARG;
+  if (empty_problem(B, H, T)) return THERIA_OK;
+  if (!q || !k || !out) return THERIA_ERR_INVALID_ARG;
+  Shape s{B, H, T, M, D, scale, 0};
+  return THERIA_DISPATCH(dtype, scores_dispatch, q, k, out, out_dtype, nullptr, s, dtype,
+                         scores::kScores, (cudaStream_t)stream);
+}
+
+int theria_sdpa_probs(const void* q, const void* k, const float* lse, float* out, int64_t B,
+                      int64_t H, int64_t T, int64_t M, int64_t D, int dtype, float scale,
+                      int causal, void* stream) {
+  if (int e = check_shape(B, H, T, M, D, dtype)) return e;
+  if (empty_problem(B, H, T)) return THERIA_OK;
+  if (!q || !k || !lse || !out) return THERIA_ERR_INVALID_ARG;
+  Shape s{B, H, T, M, D, scale, causal ? 1 : 0};
+  return THERIA_DISPATCH(dtype, scores_dispatch, q, k, out, THERIA_F32, lse, s, dtype,
+                         scores::kProbs, (cudaStream_t)stream);
 }
 
 int64_t theria_sdpa_bwd_workspace_bytes(int64_t B, int64_t H, int64_t T, int64_t M,
