@@ -14,8 +14,11 @@
 // (M = 128 query rows) in its own columns.
 // TMEM: S^T [0,64), Sd^T [64,128), dP^T [128,192), dPd^T [192,256),
 // hV [256, 256+D), hK [256+D, 256+2D), pair hQ [384, 448) for D = 64.
-// Warp roles: 0 TMA, 1 MMA issuer + TMEM owner, 2..9 compute, 10..13 hQ
-// flush.
+// Warp roles: 0 TMA, 1 issues the S-group products (and owns TMEM), 2
+// issues hK, hV and hQ, 3..10 compute, 11..14 hQ flush.  With the two groups
+// on separate threads the next tile's S-group (D = 64) runs on the tensor
+// core while the CUDA cores still work on the current tile; for D = 128 the
+// S-group waits for hQ^T to leave the S^T columns.
 #pragma once
 
 #include "sdpa_tc_bwd.cuh"
@@ -25,7 +28,8 @@ namespace tchvp {
 
 constexpr int BK = 128, BQ = 64;
 constexpr int NCOMPUTE = 256, NDQ = 128;
-constexpr int NTHREADS = 64 + NCOMPUTE + NDQ;
+constexpr int NTHREADS = 96 + NCOMPUTE + NDQ;
+constexpr int kFirstCompute = 3;
 
 template <int HD>
 struct Cfg {
@@ -41,8 +45,8 @@ struct Cfg {
   static constexpr int oDSd = oDS + NB * kP;     // dSd^T x NB (adjacent)
   static constexpr int oBar = oDSd + NB * kP;
   // kv_full, q_full[3], q_empty[3], s_full, s_read, p_full, mma2_done[2],
-  // hq_free, drain
-  static constexpr int nBar = 14;
+  // hq_free, drain[2]
+  static constexpr int nBar = 15;
   static constexpr int oTmem = oBar + nBar * 8;
   static constexpr int oAbort = oTmem + 4;
   static constexpr int kAlloc = oAbort + 4 + 1024;
@@ -89,6 +93,7 @@ hvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
     tc::mbar_init(p_full, NCOMPUTE);
     tc::mbar_init(hq_free, NDQ);
     tc::mbar_init(drain, 1);
+    tc::mbar_init(drain + 1, 1);
     *abort = 0;
     tc::fence_barrier_init();
   }
@@ -129,8 +134,8 @@ hvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       for (int t = issued > ST ? issued - ST : 0; t < issued; ++t)
         tc::mbar_wait_drain(q_full + t % ST, (t / ST) & 1);
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
+  } else if (warp == 1 || warp == 2) {
+    // ------------------------------------------------------------ MMA issuers
     if (lane == 0 && n_iter > 0) {
       constexpr int ab = tc::AbFmt<T>::v;
       constexpr uint32_t id_s = tc::idesc_f16(BK, BQ, ab, 0, 0);
@@ -155,70 +160,83 @@ hvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       const uint64_t mDSp = tc::sw128_desc(tc::smem_u32(smem + C::oDS), C::kP, 1024);
       const uint64_t mDSdp = tc::sw128_desc(tc::smem_u32(smem + C::oDSd), C::kP, 1024);
       bool ok = tc::mbar_wait(kv_full, 0, abort);
-      for (int t = 0; ok && t < n_iter; ++t) {
-        const int st = t % ST;
-        const uint32_t bo = (kPair ? (t & 1) : 0) * C::kP;  // dS/dSd buffer offset
-        const uint32_t qo = st * 3 * C::kQ, to = qo + C::kQ, wo = qo + 2 * C::kQ;
-        if (!tc::mbar_wait(q_full + st, (t / ST) & 1, abort)) break;
-        if (t >= 1 && !tc::mbar_wait(s_read, (t - 1) & 1, abort)) break;
-        if (!kPair && t >= 1 && !tc::mbar_wait(hq_free, (t - 1) & 1, abort)) break;
-        tc::tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t oa = (kk / 4) * (BK * 128) + (kk % 4) * 32;
-          const uint32_t ob = (kk / 4) * (BQ * 128) + (kk % 4) * 32;
-          const uint32_t acc = kk > 0 ? 1u : 0u;
-          tc::mma_ss(tmem + 0, tc::desc_at(kK, oa), tc::desc_at(kQ0, qo + ob), id_s, acc);
-          tc::mma_ss(tmem + 64, tc::desc_at(kK, oa), tc::desc_at(kQ0, to + ob), id_s, acc);
-          tc::mma_ss(tmem + 64, tc::desc_at(kTK, oa), tc::desc_at(kQ0, qo + ob), id_s, 1u);
-          tc::mma_ss(tmem + 128, tc::desc_at(kV, oa), tc::desc_at(kQ0, wo + ob), id_s, acc);
-          tc::mma_ss(tmem + 192, tc::desc_at(kTV, oa), tc::desc_at(kQ0, wo + ob), id_s, acc);
-        }
-        tc::mma_commit(s_full);
-        if (!tc::mbar_wait(p_full, t & 1, abort)) break;
-        tc::tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < BQ / 16; ++kk) {
-          const uint32_t ob = kk * 16 * 128;
-          const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
-          tc::mma_ss(t_hk, tc::desc_at(kDSd, bo + kk * 32), tc::desc_at(mQ0, qo + ob), id_kv,
-                     acc);                                                         // dSd^T Q
-          tc::mma_ss(t_hk, tc::desc_at(kDS, bo + kk * 32), tc::desc_at(mQ0, to + ob), id_kv,
-                     1u);                                                          // dS^T tQ
-          tc::mma_ss(t_hv, tc::desc_at(kPd, kk * 32), tc::desc_at(mQ0, wo + ob), id_kv,
-                     acc);                                                         // Pd^T W
-        }
-        if constexpr (!kPair) {
-          // hQ^T = K^T dSd^T + tK^T dS^T, into the S^T columns
-#pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk) {
-            const uint32_t o = kk * 2048;
-            tc::mma_ss(tmem, tc::desc_at(mK, o), tc::desc_at(mDSd, bo + o), id_hqt,
-                       kk > 0 ? 1u : 0u);
-            tc::mma_ss(tmem, tc::desc_at(mTK, o), tc::desc_at(mDS, bo + o), id_hqt, 1u);
-          }
-        } else if ((t & 1) || t == n_iter - 1) {
-          // hQ = dSd K + dS tK for the pair (2p, 2p+1)
-          const int p = t >> 1;
-          if (p > 0 && !tc::mbar_wait(hq_free, (p - 1) & 1, abort)) break;
+      if (warp == 1) {
+        for (int t = 0; ok && t < n_iter; ++t) {
+          const int st = t % ST;
+          const uint32_t qo = st * 3 * C::kQ, to = qo + C::kQ, wo = qo + 2 * C::kQ;
+          if (!tc::mbar_wait(q_full + st, (t / ST) & 1, abort)) break;
+          if (t >= 1 && !tc::mbar_wait(s_read, (t - 1) & 1, abort)) break;
+          // D = 128: hQ^T(t-1) sits in the S^T columns until it is flushed
+          if (!kPair && t >= 1 && !tc::mbar_wait(hq_free, (t - 1) & 1, abort)) break;
           tc::tc_fence_after();
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk) {
-            const uint32_t o = kk * 2048;
-            tc::mma_ss(t_hqp, tc::desc_at(mDSdp, o), tc::desc_at(mK, o), id_hqp,
-                       kk > 0 ? 1u : 0u);
-            tc::mma_ss(t_hqp, tc::desc_at(mDSp, o), tc::desc_at(mTK, o), id_hqp, 1u);
+          for (int kk = 0; kk < HD / 16; ++kk) {
+            const uint32_t oa = (kk / 4) * (BK * 128) + (kk % 4) * 32;
+            const uint32_t ob = (kk / 4) * (BQ * 128) + (kk % 4) * 32;
+            const uint32_t acc = kk > 0 ? 1u : 0u;
+            tc::mma_ss(tmem + 0, tc::desc_at(kK, oa), tc::desc_at(kQ0, qo + ob), id_s, acc);
+            tc::mma_ss(tmem + 64, tc::desc_at(kK, oa), tc::desc_at(kQ0, to + ob), id_s, acc);
+            tc::mma_ss(tmem + 64, tc::desc_at(kTK, oa), tc::desc_at(kQ0, qo + ob), id_s, 1u);
+            tc::mma_ss(tmem + 128, tc::desc_at(kV, oa), tc::desc_at(kQ0, wo + ob), id_s, acc);
+            tc::mma_ss(tmem + 192, tc::desc_at(kTV, oa), tc::desc_at(kQ0, wo + ob), id_s, acc);
           }
+          tc::mma_commit(s_full);
         }
-        tc::mma_commit(mma2_done + (t & 1));
-        tc::mma_commit(q_empty + st);
+        tc::mma_commit(drain);
+        tc::mbar_wait_drain(drain, 0);
+      } else {
+        for (int t = 0; ok && t < n_iter; ++t) {
+          const int st = t % ST;
+          const uint32_t bo = (kPair ? (t & 1) : 0) * C::kP;  // dS/dSd buffer offset
+          const uint32_t qo = st * 3 * C::kQ, to = qo + C::kQ, wo = qo + 2 * C::kQ;
+          if (!tc::mbar_wait(p_full, t & 1, abort)) break;
+          tc::tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < BQ / 16; ++kk) {
+            const uint32_t ob = kk * 16 * 128;
+            const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
+            tc::mma_ss(t_hk, tc::desc_at(kDSd, bo + kk * 32), tc::desc_at(mQ0, qo + ob), id_kv,
+                       acc);                                                       // dSd^T Q
+            tc::mma_ss(t_hk, tc::desc_at(kDS, bo + kk * 32), tc::desc_at(mQ0, to + ob), id_kv,
+                       1u);                                                        // dS^T tQ
+            tc::mma_ss(t_hv, tc::desc_at(kPd, kk * 32), tc::desc_at(mQ0, wo + ob), id_kv,
+                       acc);                                                       // Pd^T W
+          }
+          if constexpr (!kPair) {
+            // hQ^T = K^T dSd^T + tK^T dS^T, into the S^T columns (the compute
+            // warps loaded S^T(t) before publishing p_full)
+#pragma unroll
+            for (int kk = 0; kk < BK / 16; ++kk) {
+              const uint32_t o = kk * 2048;
+              tc::mma_ss(tmem, tc::desc_at(mK, o), tc::desc_at(mDSd, bo + o), id_hqt,
+                         kk > 0 ? 1u : 0u);
+              tc::mma_ss(tmem, tc::desc_at(mTK, o), tc::desc_at(mDS, bo + o), id_hqt, 1u);
+            }
+          } else if ((t & 1) || t == n_iter - 1) {
+            // hQ = dSd K + dS tK for the pair (2p, 2p+1)
+            const int p = t >> 1;
+            if (p > 0 && !tc::mbar_wait(hq_free, (p - 1) & 1, abort)) break;
+            tc::tc_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < BK / 16; ++kk) {
+              const uint32_t o = kk * 2048;
+              tc::mma_ss(t_hqp, tc::desc_at(mDSdp, o), tc::desc_at(mK, o), id_hqp,
+                         kk > 0 ? 1u : 0u);
+              tc::mma_ss(t_hqp, tc::desc_at(mDSp, o), tc::desc_at(mTK, o), id_hqp, 1u);
+            }
+          }
+          tc::mma_commit(mma2_done + (t & 1));
+          // the S-group products of tile t also read this stage; they were
+          // complete before the compute warps could publish p_full(t)
+          tc::mma_commit(q_empty + st);
+        }
+        tc::mma_commit(drain + 1);
+        tc::mbar_wait_drain(drain + 1, 0);
       }
-      tc::mma_commit(drain);
-      tc::mbar_wait_drain(drain, 0);
     }
-  } else if (warp < 2 + NCOMPUTE / 32) {
+  } else if (warp < kFirstCompute + NCOMPUTE / 32) {
     // ------------------------------------------------------------ compute
-    const int grp = (warp - 2) >> 2;
+    const int grp = (warp - kFirstCompute) >> 2;
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;  // TMEM lane = key row
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
