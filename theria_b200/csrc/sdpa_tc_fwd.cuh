@@ -174,9 +174,15 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
         const int st = j % STAGES;
         const bool more = j + 1 < n_tiles;
         const uint64_t dv = tc::desc_at(dv0, st * L::kKV);
+        // The operand waits of this step come first: they are normally long
+        // satisfied, but each wait still costs the issuing thread a few
+        // hundred cycles, which must not sit between a softmax publishing
+        // P and the MMAs that consume it.
+        if (!tc::mbar_wait(v_full + st, (j / STAGES) & 1, abort)) break;
+        if (more && !tc::mbar_wait(k_full + (j + 1) % STAGES, ((j + 1) / STAGES) & 1, abort))
+          break;
         for (int t = 0; t < NQT; ++t) {
           if (!tc::mbar_wait(p_full + t, j & 1, abort)) { ok = false; break; }
-          if (t == 0 && !tc::mbar_wait(v_full + st, (j / STAGES) & 1, abort)) { ok = false; break; }
           tc::tc_fence_after();
           // O_t += P_t V_j, P_t read from TMEM (packed pairs, 8 columns per 16 keys)
 #pragma unroll
@@ -185,16 +191,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
                        id_pv, (j > 0 || kk > 0) ? 1u : 0u);
           if (!more) tc::mma_commit(o_done + t);
           if (t == NQT - 1) tc::mma_commit(v_empty + st);
-          if (more) {
-            if (t == 0) {
-              if (!tc::mbar_wait(k_full + (j + 1) % STAGES, ((j + 1) / STAGES) & 1, abort)) {
-                ok = false;
-                break;
-              }
-              tc::tc_fence_after();
-            }
-            issue_s(t, j + 1);
-          }
+          if (more) issue_s(t, j + 1);
         }
       }
       // Every MMA issued above completes before TMEM is freed.
