@@ -2,6 +2,9 @@
 // problem descriptor every kernel receives, and launch-error plumbing.
 #pragma once
 
+#include <cstdio>
+#include <cstdlib>
+
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
@@ -70,9 +73,14 @@ inline std::atomic<long long>& launch_counter() {
 }
 
 // Call right after each kernel launch: counts it and maps the launch error.
+// With THERIA_DEBUG set in the environment the CUDA error text goes to stderr.
 inline int launch_status() {
   launch_counter().fetch_add(1, std::memory_order_relaxed);
-  return cudaGetLastError() == cudaSuccess ? THERIA_OK : THERIA_ERR_LAUNCH;
+  const cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) return THERIA_OK;
+  static const bool debug = std::getenv("THERIA_DEBUG") != nullptr;
+  if (debug) std::fprintf(stderr, "theria: kernel launch failed: %s\n", cudaGetErrorString(e));
+  return THERIA_ERR_LAUNCH;
 }
 
 inline int64_t elem_size(int dtype) { return dtype == THERIA_F32 ? 4 : 2; }
