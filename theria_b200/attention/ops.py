@@ -19,6 +19,11 @@ import torch
 from theria_b200 import _lib
 
 _ALLOWED_DTYPES = (torch.float16, torch.bfloat16, torch.float32)
+
+# Each operator is one opaque library call: torch.compile (dynamo) runs it
+# eagerly between the graphs it captures around it instead of tracing into
+# the ctypes call.
+_opaque = torch.compiler.disable
 MAX_HEAD_DIM = 128
 
 
@@ -70,6 +75,7 @@ def _check_lse(lse, B, H, T):
         raise AssertionError("lse must be float32 forward stats with shape (B,H,T)")
 
 
+@_opaque
 def forward(q, k, v, *, causal=False, scale=None, out_dtype=None, need_lse=True):
     """O = softmax(scale q k^T) v and the row logsumexp.
 
@@ -108,6 +114,7 @@ def check_qk(q, k, what):
     return B, H, T, k.shape[2], D
 
 
+@_opaque
 def scores(q, k, *, scale=1.0, out_dtype=torch.float32):
     """Dense S = scale q k^T as [B, H, T, M] (fp32 accumulation)."""
     B, H, T, M, D = check_qk(q, k, "theria scores")
@@ -123,6 +130,7 @@ def scores(q, k, *, scale=1.0, out_dtype=torch.float32):
     return out
 
 
+@_opaque
 def probs(q, k, *, causal=False, scale=None, lse=None):
     """Dense P = softmax(scale q k^T) as float32 [B, H, T, M].
 
@@ -144,6 +152,7 @@ def probs(q, k, *, causal=False, scale=None, lse=None):
     return out
 
 
+@_opaque
 def backward(q, k, v, dout, lse, *, o=None, causal=False, scale=None,
              need=(True, True, True)):
     """dQ, dK, dV of <O, dout>; entries of ``need`` that are False return None."""
@@ -172,6 +181,7 @@ def backward(q, k, v, dout, lse, *, o=None, causal=False, scale=None,
     return dq, dk, dv
 
 
+@_opaque
 def jvp(q, k, v, tq, tk, tv, lse, *, causal=False, scale=None):
     """Tangent of O along (tq, tk, tv), P rebuilt from the saved lse."""
     B, H, T, M, D = check_qkv(q, k, v, "theria JVP")
@@ -191,6 +201,7 @@ def jvp(q, k, v, tq, tk, tv, lse, *, causal=False, scale=None):
     return o_tan
 
 
+@_opaque
 def hvp(q, k, v, w, lse, tq, tk, tv, *, causal=False, scale=None,
         need=(True, True, True, True)):
     """H u of L = <O, w> along u = (tq, tk, tv), plus J u.
