@@ -9,8 +9,9 @@
 //              P^T  = exp(s S^T - LSE),  dS^T = P^T (dP^T - z)   (CUDA cores,
 //                     one key row per thread, 16-bit SW128 tiles in smem)
 //              dV  += P^T dO_t,  dK += dS^T Q_t       (TMEM accumulators)
-//              dQ   = dS K, added to the fp32 accumulator dQacc with
-//                     global reductions; dK, dV are stored once at the end.
+//              dQ   = dS K, staged in shared memory and added to the fp32
+//                     accumulator dQacc by TMA bulk reductions; dK, dV are
+//                     stored once at the end.
 //   finish   dQ = dQacc in the input dtype (dQacc is pre-scaled)
 // TMEM (512 columns): S^T [0,64) and dP^T [64,128), released as soon as the
 // CUDA cores have loaded them; dV [128, 128+D); dK [128+D, 128+2D).
@@ -48,8 +49,10 @@ struct Smem {
   // complete, so the ring must cover that latency plus the TMA refill.
   static constexpr int QST = HD == 128 ? 3 : 4;
   static constexpr int kP = BK * BQ * 2;    // one dS^T buffer [key][q]
-  // fp32 dQ tile [q][d] staged for the bulk reduction (D = 128 only)
-  static constexpr int kStage = HD == 128 ? BQ * HD * 4 : 0;
+  // fp32 dQ staged for the bulk reduction: 64 query rows of dQ^T as rows
+  // [q][d] (D = 128), or a pair's 128 query rows of dQ as two 128-byte-swizzled
+  // halves [q][32 d] (D = 64); 32 KB either way
+  static constexpr int kStage = 32768;
   static constexpr int oK = 0;
   static constexpr int oV = oK + kKV;
   static constexpr int oQ = oV + kKV;       // QST stages
@@ -109,7 +112,8 @@ template <typename T, int HD, bool CAUSAL>
 __global__ void __launch_bounds__(NTHREADS, 1)
 bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
            const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
-           const float* __restrict__ lse, const float* __restrict__ z,
+           const __grid_constant__ CUtensorMap tm_dq, const float* __restrict__ lse,
+           const float* __restrict__ z,
            float* __restrict__ dq_acc, T* __restrict__ dk, T* __restrict__ dv, int Tq, int M,
            float scale, float scale_log2) {
   using L = Smem<HD>;
@@ -443,22 +447,47 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
         }
         if (!__shfl_sync(0xffffffffu, staged, 0)) break;
       } else {
-        // dQ of the pair ending at tile t: lane = query row, 64 head dims
-        const int q = tile_of(t & ~1) * BQ + r;
-#pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
-          float v[32];
-          tc::tmem_ld32(t_dqp + lane_off + c * 32, v);
-          if (q < Tq) {
-            float* dst = dq_acc + (row_base + q) * HD + c * 32;
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-              red_add_v4(dst + 4 * i, v[4 * i] * scale, v[4 * i + 1] * scale,
-                         v[4 * i + 2] * scale, v[4 * i + 3] * scale);
-          }
-        }
+        // dQ of the pair ending at tile t (lane = query row, 64 head dims):
+        // read out of TMEM, release the buffer, stage it scaled in two
+        // 128-byte-swizzled halves [q][32 d] (the swizzle spreads a warp's
+        // 16-byte stores over all banks) and add the pair's rows to dQacc with
+        // two bulk tensor reductions (rows past the end are clipped).
+        const int qb = tile_of(t & ~1) * BQ;
+        float v0[32], v1[32];
+        tc::tmem_ld32(t_dqp + lane_off, v0);
+        tc::tmem_ld32(t_dqp + lane_off + 32, v1);
         tc::tc_fence_before();
         tc::mbar_arrive(dq_free);
+        const int pi = t >> 1;  // pair index: phase of the staging barriers
+        if (bulk_issuer) {
+          tc::bulk_wait_read_all();
+          tc::mbar_arrive(stage_free);
+        }
+        if (!wait(stage_free, pi & 1)) break;
+        const uint32_t srow = tc::smem_u32(smem + L::oStage) + (uint32_t)r * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const uint32_t off = (uint32_t)((c ^ (r & 7)) << 4);
+          tc::st_shared_v4(srow + off, __float_as_uint(v0[4 * c] * scale),
+                           __float_as_uint(v0[4 * c + 1] * scale),
+                           __float_as_uint(v0[4 * c + 2] * scale),
+                           __float_as_uint(v0[4 * c + 3] * scale));
+          tc::st_shared_v4(srow + 16384 + off, __float_as_uint(v1[4 * c] * scale),
+                           __float_as_uint(v1[4 * c + 1] * scale),
+                           __float_as_uint(v1[4 * c + 2] * scale),
+                           __float_as_uint(v1[4 * c + 3] * scale));
+        }
+        tc::fence_proxy_async_smem();
+        tc::mbar_arrive(stage_full);
+        bool staged = true;
+        if (bulk_issuer) {
+          staged = tc::mbar_wait(stage_full, pi & 1, abort);
+          if (staged) {
+            tc::bulk_tensor_reduce_add_3d(&tm_dq, smem + L::oStage, 0, qb, bh);
+            tc::bulk_tensor_reduce_add_3d(&tm_dq, smem + L::oStage + 16384, 32, qb, bh);
+          }
+        }
+        if (!__shfl_sync(0xffffffffu, staged, 0)) break;
       }
     }
     // the last reductions must finish before the CTA (and its staging

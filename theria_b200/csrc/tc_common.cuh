@@ -110,6 +110,18 @@ __device__ __forceinline__ void bulk_reduce_add_f32(float* dst, const void* src,
       "r"(smem_u32(src)), "r"(bytes)
       : "memory");
 }
+// Tiled tensor reduction: the box at (x, y, z) of `map` += the (swizzled)
+// shared-memory tile at src, as one bulk-async group.  x * element size must
+// be a multiple of 16 bytes and no coordinate negative.
+__device__ __forceinline__ void bulk_tensor_reduce_add_3d(const CUtensorMap* map, const void* src,
+                                                          int x, int y, int z) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group"
+      " [%0, {%2, %3, %4}], [%1];\n\t"
+      "cp.async.bulk.commit_group;" ::"l"(reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
 // Wait until every bulk group of this thread has finished reading shared memory.
 __device__ __forceinline__ void bulk_wait_read_all() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");

@@ -50,6 +50,22 @@ inline bool make_map_3d(CUtensorMap* map, const void* base, int dtype, int64_t b
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 3-D fp32 map over [B*H, rows, hd] with box {32 floats (128 B), box_rows, 1}
+// and 128-byte swizzle: the destination of bulk tensor reductions from a
+// swizzled shared-memory stage.
+inline bool make_map_3d_f32(CUtensorMap* map, void* base, int64_t bh, int64_t rows, int64_t hd,
+                            uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)hd, (cuuint64_t)rows, (cuuint64_t)bh};
+  cuuint64_t strides[2] = {(cuuint64_t)(hd * 4), (cuuint64_t)(rows * hd * 4)};
+  cuuint32_t box[3] = {32, box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // The tensor-core kernels take 16-bit inputs with head dim 64 or 128 and

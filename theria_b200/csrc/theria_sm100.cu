@@ -5,6 +5,7 @@
 // workspace carving and kernel selection for each entry point.
 #include <algorithm>
 #include <cstdio>
+#include <cstring>
 #include <type_traits>
 #include <initializer_list>
 #include <mutex>
@@ -266,13 +267,14 @@ int64_t tc_bwd_ws(const Shape& s) {
 
 template <typename T, int HD, bool CAUSAL>
 int tc_bwd_launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
-                  const CUtensorMap& mdo, const float* lse, const float* z, float* dq_acc,
-                  void* dk, void* dv, const Shape& s, cudaStream_t st) {
+                  const CUtensorMap& mdo, const CUtensorMap& mdq, const float* lse,
+                  const float* z, float* dq_acc, void* dk, void* dv, const Shape& s,
+                  cudaStream_t st) {
   auto kern = tcbwd::bwd_kernel<T, HD, CAUSAL>;
   constexpr int smem = tcbwd::Smem<HD>::kAlloc;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   dim3 grid((unsigned)((s.M + tcbwd::BK - 1) / tcbwd::BK), (unsigned)(s.B * s.H));
-  kern<<<grid, tcbwd::NTHREADS, smem, st>>>(mq, mk, mv, mdo, lse, z, dq_acc, (T*)dk, (T*)dv,
+  kern<<<grid, tcbwd::NTHREADS, smem, st>>>(mq, mk, mv, mdo, mdq, lse, z, dq_acc, (T*)dk, (T*)dv,
                                             (int)s.T, (int)s.M, s.scale,
                                             s.scale * 1.4426950408889634f);
   return launch_status();
@@ -293,6 +295,10 @@ int tc_bwd(const void* q, const void* k, const void* v, const void* o, int o_dty
   float* z = (float*)ws;
   float* dq_acc = (float*)((char*)ws + align_up(bh * s.T * 4));
   const int64_t rows = bh * s.T;
+  // D = 64 adds its dQ tiles through a swizzled fp32 map of the accumulator
+  CUtensorMap mdq;
+  std::memset(&mdq, 0, sizeof(mdq));
+  if (s.D == 64 && !tc::make_map_3d_f32(&mdq, dq_acc, bh, s.T, s.D, 2 * tcbwd::BQ)) return -1;
   if (o != nullptr) {
     tcbwd::prep_kernel<T><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(
         o, o_dtype == THERIA_F32, (const T*)dout, z, dq_acc, rows, (int)s.D);
@@ -308,11 +314,11 @@ int tc_bwd(const void* q, const void* k, const void* v, const void* o, int o_dty
   }
   int e;
   if (s.D == 64)
-    e = s.causal ? tc_bwd_launch<T, 64, true>(mq, mk, mv, mdo, lse, z, dq_acc, dk, dv, s, st)
-                 : tc_bwd_launch<T, 64, false>(mq, mk, mv, mdo, lse, z, dq_acc, dk, dv, s, st);
+    e = s.causal ? tc_bwd_launch<T, 64, true>(mq, mk, mv, mdo, mdq, lse, z, dq_acc, dk, dv, s, st)
+                 : tc_bwd_launch<T, 64, false>(mq, mk, mv, mdo, mdq, lse, z, dq_acc, dk, dv, s, st);
   else
-    e = s.causal ? tc_bwd_launch<T, 128, true>(mq, mk, mv, mdo, lse, z, dq_acc, dk, dv, s, st)
-                 : tc_bwd_launch<T, 128, false>(mq, mk, mv, mdo, lse, z, dq_acc, dk, dv, s, st);
+    e = s.causal ? tc_bwd_launch<T, 128, true>(mq, mk, mv, mdo, mdq, lse, z, dq_acc, dk, dv, s, st)
+                 : tc_bwd_launch<T, 128, false>(mq, mk, mv, mdo, mdq, lse, z, dq_acc, dk, dv, s, st);
   if (e) return e;
   if (dq != nullptr) {
     const int64_t n = rows * s.D;
