@@ -33,7 +33,7 @@ constexpr int kFirstCompute = 3;
 
 template <int HD>
 struct Cfg {
-  static constexpr int ST = HD == 64 ? 3 : 1;  // Q/tQ/W ring depth (what smem allows)
+  static constexpr int ST = HD == 64 ? 2 : 1;  // Q/tQ/W ring depth (what smem allows)
   static constexpr int kKV = BK * HD * 2;
   static constexpr int kQ = BQ * HD * 2;
   static constexpr int kP = BK * BQ * 2;
@@ -43,10 +43,14 @@ struct Cfg {
   static constexpr int NB = HD == 64 ? 2 : 1;   // dS/dSd buffers (2: pair operand)
   static constexpr int oDS = oPd + kP;           // dS^T  x NB (adjacent)
   static constexpr int oDSd = oDS + NB * kP;     // dSd^T x NB (adjacent)
-  static constexpr int oBar = oDSd + NB * kP;
+  // fp32 hQ of a pair of query tiles, staged as two 128-byte-swizzled halves
+  // [128 q][32 d] for the bulk tensor reduction (D = 64 only)
+  static constexpr int oStage = oDSd + NB * kP;
+  static constexpr int kStage = HD == 64 ? 32768 : 0;
+  static constexpr int oBar = oStage + kStage;
   // kv_full, q_full[3], q_empty[3], s_full, s_read, p_full, mma2_done[2],
-  // hq_free, drain[2]
-  static constexpr int nBar = 15;
+  // hq_free, drain[2], stage_free, stage_full
+  static constexpr int nBar = 17;
   static constexpr int oTmem = oBar + nBar * 8;
   static constexpr int oAbort = oTmem + 4;
   static constexpr int kAlloc = oAbort + 4 + 1024;
@@ -57,7 +61,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 hvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_tq,
            const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_k,
            const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_tk,
-           const __grid_constant__ CUtensorMap tm_tv, const float* __restrict__ lse,
+           const __grid_constant__ CUtensorMap tm_tv, const __grid_constant__ CUtensorMap tm_hq,
+           const float* __restrict__ lse,
            const float* __restrict__ stats, int64_t n_rows_total, float* __restrict__ hq_acc,
            T* __restrict__ hk, T* __restrict__ hv, int Tq, int M, float scale,
            float scale_log2) {
@@ -70,7 +75,7 @@ hvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::oBar);
   uint64_t *kv_full = bars, *q_full = bars + 1, *q_empty = bars + 4, *s_full = bars + 7,
            *s_read = bars + 8, *p_full = bars + 9, *mma2_done = bars + 10, *hq_free = bars + 12,
-           *drain = bars + 13;
+           *drain = bars + 13, *stage_free = bars + 15, *stage_full = bars + 16;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::oTmem);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + C::oAbort);
 
@@ -94,6 +99,8 @@ hvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
     tc::mbar_init(hq_free, NDQ);
     tc::mbar_init(drain, 1);
     tc::mbar_init(drain + 1, 1);
+    tc::mbar_init(stage_free, 1);
+    tc::mbar_init(stage_full, NDQ);
     *abort = 0;
     tc::fence_barrier_init();
   }
@@ -347,6 +354,7 @@ hvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
     const int r = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const size_t row_base = (size_t)bh * Tq;
+    const bool bulk_issuer = warp == kFirstCompute + NCOMPUTE / 32 && lane == 0;
     auto wait = [&](uint64_t* bar, uint32_t parity) {
       return __all_sync(0xffffffffu, tc::mbar_wait(bar, parity, abort));
     };
@@ -367,23 +375,53 @@ hvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
           }
         }
       } else {
-        const int q = (i_begin + (t & ~1)) * BQ + r;
-#pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
-          float v[32];
-          tc::tmem_ld32(t_hqp + lane_off + c * 32, v);
-          if (q < Tq) {
-            float* dst = hq_acc + (row_base + q) * HD + c * 32;
+        // hQ of the pair ending at tile t (lane = query row, 64 head dims):
+        // read out of TMEM, release the buffer, stage it scaled in two
+        // 128-byte-swizzled halves and add the pair's rows to hQacc with two
+        // bulk tensor reductions (rows past the end are clipped).
+        const int qb = (i_begin + (t & ~1)) * BQ;
+        float v0[32], v1[32];
+        tc::tmem_ld32(t_hqp + lane_off, v0);
+        tc::tmem_ld32(t_hqp + lane_off + 32, v1);
+        tc::tc_fence_before();
+        tc::mbar_arrive(hq_free);
+        const int pi = t >> 1;  // pair index: phase of the staging barriers
+        if (bulk_issuer) {
+          tc::bulk_wait_read_all();
+          tc::mbar_arrive(stage_free);
+        }
+        if (!wait(stage_free, pi & 1)) break;
+        const uint32_t srow = tc::smem_u32(smem + C::oStage) + (uint32_t)r * 128;
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-              tcbwd::red_add_v4(dst + 4 * i, v[4 * i] * scale, v[4 * i + 1] * scale,
-                                v[4 * i + 2] * scale, v[4 * i + 3] * scale);
+        for (int c = 0; c < 8; ++c) {
+          const uint32_t off = (uint32_t)((c ^ (r & 7)) << 4);
+          tc::st_shared_v4(srow + off, __float_as_uint(v0[4 * c] * scale),
+                           __float_as_uint(v0[4 * c + 1] * scale),
+                           __float_as_uint(v0[4 * c + 2] * scale),
+                           __float_as_uint(v0[4 * c + 3] * scale));
+          tc::st_shared_v4(srow + 16384 + off, __float_as_uint(v1[4 * c] * scale),
+                           __float_as_uint(v1[4 * c + 1] * scale),
+                           __float_as_uint(v1[4 * c + 2] * scale),
+                           __float_as_uint(v1[4 * c + 3] * scale));
+        }
+        tc::fence_proxy_async_smem();
+        tc::mbar_arrive(stage_full);
+        bool staged = true;
+        if (bulk_issuer) {
+          staged = tc::mbar_wait(stage_full, pi & 1, abort);
+          if (staged) {
+            tc::bulk_tensor_reduce_add_3d(&tm_hq, smem + C::oStage, 0, qb, bh);
+            tc::bulk_tensor_reduce_add_3d(&tm_hq, smem + C::oStage + 16384, 32, qb, bh);
           }
         }
+        if (!__shfl_sync(0xffffffffu, staged, 0)) break;
+        continue;
       }
       tc::tc_fence_before();
       tc::mbar_arrive(hq_free);
     }
+    // the last reductions must finish before the CTA (and its stage) goes away
+    if (bulk_issuer) tc::bulk_wait_all();
   }
   // ------------------------------------------------------------ teardown
   tc::tc_fence_before();

@@ -380,7 +380,8 @@ int tc_hvp_launch(const CUtensorMap* m, const float* lse, const float* stats, fl
   auto kern = tchvp::hvp_kernel<T, HD, CAUSAL>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kAlloc);
   dim3 grid((unsigned)((s.M + tchvp::BK - 1) / tchvp::BK), (unsigned)(s.B * s.H));
-  kern<<<grid, tchvp::NTHREADS, C::kAlloc, st>>>(m[0], m[1], m[2], m[3], m[4], m[5], m[6], lse,
+  kern<<<grid, tchvp::NTHREADS, C::kAlloc, st>>>(m[0], m[1], m[2], m[3], m[4], m[5], m[6], m[7],
+                                                 lse,
                                                  stats, s.B * s.H * s.T, hq_acc, (T*)hk,
                                                  (T*)hv, (int)s.T, (int)s.M, s.scale,
                                                  s.scale * 1.4426950408889634f);
@@ -393,7 +394,7 @@ template <typename T>
 int tc_hvp(const void* q, const void* k, const void* v, const void* w, const float* lse,
            const void* tq, const void* tk, const void* tv, void* hq, void* hk, void* hv,
            void* o_tan, void* ws, const Shape& s, int dtype, cudaStream_t st) {
-  CUtensorMap m[7];
+  CUtensorMap m[8];
   const int64_t bh = s.B * s.H;
   const void* src[7] = {q, tq, w, k, v, tk, tv};
   for (int i = 0; i < 7; ++i)
@@ -402,6 +403,9 @@ int tc_hvp(const void* q, const void* k, const void* v, const void* w, const flo
       return -1;
   float* stats = (float*)ws;
   float* hq_acc = (float*)((char*)ws + align_up(3 * bh * s.T * 4));
+  // D = 64 adds its hQ tiles through a swizzled fp32 map of the accumulator
+  std::memset(&m[7], 0, sizeof(m[7]));
+  if (s.D == 64 && !tc::make_map_3d_f32(&m[7], hq_acc, bh, s.T, s.D, 2 * tchvp::BQ)) return -1;
   int e = tc_jvp<T>(q, k, v, tq, tk, tv, w, lse, o_tan, stats, s, dtype, st);
   if (e != 0) return e;
   const int64_t n = bh * s.T * s.D;
