@@ -52,10 +52,10 @@ CFG3 = dict(B=2, H=8, N=2048, D=64)
 
 # DRAM bytes per launch of the backward's main kernel from one ncu capture
 # (dram__bytes_read.sum + dram__bytes_write.sum), keyed by workload; None
-# until a capture exists for the kernel that runs.  Summaries: profiles/.
-# profiles/sdpa_fwdbwd_cfg2.md: bwd_kernel at B=1 read 101.3 MB and wrote
-# 20.7 MB; traffic grows with the (b, h) units, so x4 for B=4.
-NCU_TRAFFIC_BYTES: dict[str, float | None] = {"cfg2": 4 * (101.3e6 + 20.7e6)}
+# until a capture exists for the kernel that runs.  The capture of
+# bwd_kernel at B=1 H=16 N=4096 D=128 read 101.3 MB and wrote 22.7 MB;
+# traffic grows with the (b, h) units, so x4 for B=4.
+NCU_TRAFFIC_BYTES: dict[str, float | None] = {"cfg2": 4 * (101.3e6 + 22.7e6)}
 
 
 def flops(kind, B, H, N, D, causal=False):
