@@ -38,10 +38,16 @@ extern "C" {
 #define THERIA_ERR_SCRATCH_LIMIT 6 /* problem exceeds the fixed scratch of
                                       theria_sdpa_bwd_noalloc            */
 
-/* element types */
+/* element types.  THERIA_F64 (double precision throughout, for
+ * gradcheck-style verification) runs only in the whole-head kernels: the
+ * forward, backward, JVP and HVP accept it for T, M <= 64 and D <= 64 where
+ * the head fits in shared memory as doubles, and return
+ * THERIA_ERR_UNSUPPORTED otherwise; lse stays float32.  The dense score and
+ * probability entry points do not take it. */
 #define THERIA_F32 0
 #define THERIA_F16 1
 #define THERIA_BF16 2
+#define THERIA_F64 3
 
 /* largest head dimension any entry point accepts */
 #define THERIA_MAX_HEAD_DIM 128

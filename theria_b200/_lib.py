@@ -24,8 +24,8 @@ THERIA_ERR_DEVICE_TIMEOUT = 5
 THERIA_ERR_SCRATCH_LIMIT = 6
 NOALLOC_SCRATCH_BYTES = 4 * 1024 * 1024
 
-F32, F16, BF16 = 0, 1, 2
-DTYPE_CODE = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
+F32, F16, BF16, F64 = 0, 1, 2, 3
+DTYPE_CODE = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16, torch.float64: F64}
 
 _vp = ctypes.c_void_p
 _i64 = ctypes.c_int64

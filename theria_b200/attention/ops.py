@@ -18,7 +18,9 @@ import torch
 
 from theria_b200 import _lib
 
-_ALLOWED_DTYPES = (torch.float16, torch.bfloat16, torch.float32)
+# float64 runs in double precision in the whole-head kernels only (T, M, D
+# <= 64; other shapes raise), for gradcheck-style verification.
+_ALLOWED_DTYPES = (torch.float16, torch.bfloat16, torch.float32, torch.float64)
 
 # Each operator is one opaque library call: torch.compile (dynamo) runs it
 # eagerly between the graphs it captures around it instead of tracing into

@@ -27,7 +27,9 @@ constexpr int64_t kAlign = 256;
 
 int64_t align_up(int64_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 
-bool valid_dtype(int dt) { return dt == THERIA_F32 || dt == THERIA_F16 || dt == THERIA_BF16; }
+bool valid_dtype(int dt) {
+  return dt == THERIA_F32 || dt == THERIA_F16 || dt == THERIA_BF16 || dt == THERIA_F64;
+}
 
 // Shared argument checks; returns THERIA_OK or an error status.
 int check_shape(int64_t B, int64_t H, int64_t T, int64_t M, int64_t D, int dtype) {
@@ -166,24 +168,33 @@ bool small_eligible(const Shape& s) {
   return s.T <= small::MAXN && s.M <= small::MAXN && s.D <= small::MAXD && s.B * s.H < (1ll << 31);
 }
 
+// fp64 runs only in the whole-head kernels, in double precision throughout,
+// and only where the head (inputs and score-shaped matrices, as doubles)
+// fits in one CTA's shared memory.
+constexpr size_t kMaxSmem = 227 * 1024;
+bool f64_fits(const Shape& s, int n_q, int n_k, int n_s) {
+  return small_eligible(s) &&
+         small::smem_bytes((int)s.T, (int)s.M, (int)s.D, n_q, n_k, n_s, sizeof(double)) <= kMaxSmem;
+}
+
 template <typename K>
 void small_setup(K kern, size_t bytes) {
   if (bytes > 48 * 1024)
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
 }
 
-template <typename T>
+template <typename T, typename A = float>
 int small_fwd(const void* q, const void* k, const void* v, void* o, int o_dtype, float* lse,
               const Shape& s, cudaStream_t st) {
-  const size_t sm = small::smem_bytes((int)s.T, (int)s.M, (int)s.D, 1, 2, 1);
+  const size_t sm = small::smem_bytes((int)s.T, (int)s.M, (int)s.D, 1, 2, 1, sizeof(A));
   const unsigned grid = (unsigned)(s.B * s.H);
   if (o_dtype == THERIA_F32) {
-    auto kern = small::fwd_kernel<T, float>;
+    auto kern = small::fwd_kernel<T, float, A>;
     small_setup(kern, sm);
     kern<<<grid, small::NTHREADS, sm, st>>>((const T*)q, (const T*)k, (const T*)v, (float*)o,
                                             lse, s);
   } else {
-    auto kern = small::fwd_kernel<T, T>;
+    auto kern = small::fwd_kernel<T, T, A>;
     small_setup(kern, sm);
     kern<<<grid, small::NTHREADS, sm, st>>>((const T*)q, (const T*)k, (const T*)v, (T*)o, lse,
                                             s);
@@ -191,22 +202,22 @@ int small_fwd(const void* q, const void* k, const void* v, void* o, int o_dtype,
   return launch_status();
 }
 
-template <typename T>
+template <typename T, typename A = float>
 int small_bwd(const void* q, const void* k, const void* v, const void* dout, const float* lse,
               void* dq, void* dk, void* dv, const Shape& s, cudaStream_t st) {
-  const size_t sm = small::smem_bytes((int)s.T, (int)s.M, (int)s.D, 2, 2, 2);
-  auto kern = small::bwd_kernel<T>;
+  const size_t sm = small::smem_bytes((int)s.T, (int)s.M, (int)s.D, 2, 2, 2, sizeof(A));
+  auto kern = small::bwd_kernel<T, A>;
   small_setup(kern, sm);
   kern<<<(unsigned)(s.B * s.H), small::NTHREADS, sm, st>>>(
       (const T*)q, (const T*)k, (const T*)v, (const T*)dout, lse, (T*)dq, (T*)dk, (T*)dv, s);
   return launch_status();
 }
 
-template <typename T>
+template <typename T, typename A = float>
 int small_jvp(const void* q, const void* k, const void* v, const void* tq, const void* tk,
               const void* tv, const float* lse, void* o_tan, const Shape& s, cudaStream_t st) {
-  const size_t sm = small::smem_bytes((int)s.T, (int)s.M, (int)s.D, 2, 4, 2);
-  auto kern = small::jvp_kernel<T>;
+  const size_t sm = small::smem_bytes((int)s.T, (int)s.M, (int)s.D, 2, 4, 2, sizeof(A));
+  auto kern = small::jvp_kernel<T, A>;
   small_setup(kern, sm);
   kern<<<(unsigned)(s.B * s.H), small::NTHREADS, sm, st>>>(
       (const T*)q, (const T*)k, (const T*)v, (const T*)tq, (const T*)tk, (const T*)tv, lse,
@@ -214,12 +225,12 @@ int small_jvp(const void* q, const void* k, const void* v, const void* tq, const
   return launch_status();
 }
 
-template <typename T>
+template <typename T, typename A = float>
 int small_hvp(const void* q, const void* k, const void* v, const void* w, const float* lse,
               const void* tq, const void* tk, const void* tv, void* hq, void* hk, void* hv,
               void* o_tan, const Shape& s, cudaStream_t st) {
-  const size_t sm = small::smem_bytes((int)s.T, (int)s.M, (int)s.D, 3, 4, 4);
-  auto kern = small::hvp_kernel<T>;
+  const size_t sm = small::smem_bytes((int)s.T, (int)s.M, (int)s.D, 3, 4, 4, sizeof(A));
+  auto kern = small::hvp_kernel<T, A>;
   small_setup(kern, sm);
   kern<<<(unsigned)(s.B * s.H), small::NTHREADS, sm, st>>>(
       (const T*)q, (const T*)k, (const T*)v, (const T*)w, lse, (const T*)tq, (const T*)tk,
@@ -519,6 +530,9 @@ int theria_sdpa_fwd(const void* q, const void* k, const void* v, void* o, int o_
   if (!q || !k || !v || !o) return THERIA_ERR_INVALID_ARG;
   Shape s{B, H, T, M, D, scale, causal ? 1 : 0};
   cudaStream_t st = (cudaStream_t)stream;
+  if (dtype == THERIA_F64)
+    return f64_fits(s, 1, 2, 1) ? small_fwd<double, double>(q, k, v, o, o_dtype, lse, s, st)
+                                : THERIA_ERR_UNSUPPORTED;
   if (small_eligible(s)) return THERIA_DISPATCH(dtype, small_fwd, q, k, v, o, o_dtype, lse, s, st);
   if (use_tc(dtype, s, {q, k, v, o})) {
     int e = dtype == THERIA_BF16 ? tc_fwd<__nv_bfloat16>(q, k, v, o, o_dtype, lse, s, dtype, st)
@@ -533,6 +547,7 @@ int theria_sdpa_scores(const void* q, const void* k, void* out, int out_dtype, i
                        void* stream) {
   if (int e = check_shape(B, H, T, M, D, dtype)) return e;
   if (out_dtype != THERIA_F32 && out_dtype != dtype) return THERIA_ERR_INVALID_ARG;
+  if (dtype == THERIA_F64) return THERIA_ERR_UNSUPPORTED;
   if (empty_problem(B, H, T)) return THERIA_OK;
   if (!q || !k || !out) return THERIA_ERR_INVALID_ARG;
   Shape s{B, H, T, M, D, scale, 0};
@@ -544,6 +559,7 @@ int theria_sdpa_probs(const void* q, const void* k, const float* lse, float* out
                       int64_t H, int64_t T, int64_t M, int64_t D, int dtype, float scale,
                       int causal, void* stream) {
   if (int e = check_shape(B, H, T, M, D, dtype)) return e;
+  if (dtype == THERIA_F64) return THERIA_ERR_UNSUPPORTED;
   if (empty_problem(B, H, T)) return THERIA_OK;
   if (!q || !k || !lse || !out) return THERIA_ERR_INVALID_ARG;
   Shape s{B, H, T, M, D, scale, causal ? 1 : 0};
@@ -578,6 +594,9 @@ int theria_sdpa_bwd(const void* q, const void* k, const void* v, const void* o, 
   Shape s{B, H, T, M, D, scale, causal ? 1 : 0};
   if (!workspace || workspace_bytes < simt_bwd_ws(s)) return THERIA_ERR_WORKSPACE;
   cudaStream_t st = (cudaStream_t)stream;
+  if (dtype == THERIA_F64)
+    return f64_fits(s, 2, 2, 2) ? small_bwd<double, double>(q, k, v, dout, lse, dq, dk, dv, s, st)
+                                : THERIA_ERR_UNSUPPORTED;
   if (small_eligible(s))
     return THERIA_DISPATCH(dtype, small_bwd, q, k, v, dout, lse, dq, dk, dv, s, st);
   // The tensor-core path needs the larger workspace; a caller that passes
@@ -603,6 +622,10 @@ int theria_sdpa_jvp(const void* q, const void* k, const void* v, const void* tq,
   if (!q || !k || !v || !tq || !tk || !tv || !lse || !o_tan) return THERIA_ERR_INVALID_ARG;
   Shape s{B, H, T, M, D, scale, causal ? 1 : 0};
   cudaStream_t st = (cudaStream_t)stream;
+  if (dtype == THERIA_F64)
+    return f64_fits(s, 2, 4, 2)
+               ? small_jvp<double, double>(q, k, v, tq, tk, tv, lse, o_tan, s, st)
+               : THERIA_ERR_UNSUPPORTED;
   if (small_eligible(s))
     return THERIA_DISPATCH(dtype, small_jvp, q, k, v, tq, tk, tv, lse, o_tan, s, st);
   if (use_tc(dtype, s, {q, k, v, tq, tk, tv, o_tan})) {
@@ -627,6 +650,10 @@ int theria_sdpa_hvp(const void* q, const void* k, const void* v, const void* w,
   Shape s{B, H, T, M, D, scale, causal ? 1 : 0};
   if (!workspace || workspace_bytes < simt_hvp_ws(s)) return THERIA_ERR_WORKSPACE;
   cudaStream_t st = (cudaStream_t)stream;
+  if (dtype == THERIA_F64)
+    return f64_fits(s, 3, 4, 4) ? small_hvp<double, double>(q, k, v, w, lse, tq, tk, tv, hq, hk,
+                                                            hv, o_tan, s, st)
+                                : THERIA_ERR_UNSUPPORTED;
   if (small_eligible(s))
     return THERIA_DISPATCH(dtype, small_hvp, q, k, v, w, lse, tq, tk, tv, hq, hk, hv, o_tan, s,
                            st);
