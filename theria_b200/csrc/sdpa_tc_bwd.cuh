@@ -249,6 +249,14 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
         const uint64_t mDSpair = tc::sw128_desc(a_ds, L::kP, 1024);
         for (int t = 0; ok && t < n_iter; ++t) {
           const int b = t & 1;
+          // D = 64: the pair-dQ buffer wait comes first.  It is normally
+          // satisfied, but any wait costs this (MMA-issuing) thread a few
+          // hundred cycles, better spent while the compute warps still produce
+          // P^T / dS^T.  (For D = 128 the previous dQ^T flush can still be
+          // running here, and waiting for it would hold back dV/dK.)
+          if (kPairDq && ((t & 1) || t == n_iter - 1) && (t >> 1) > 0 &&
+              !tc::mbar_wait(dq_free, ((t >> 1) - 1) & 1, abort))
+            break;
           if (!tc::mbar_wait(p_full + b, (t >> 1) & 1, abort)) break;
           tc::tc_fence_after();
           const uint32_t pbo = b * L::kP;  // this tile's dS^T buffer offset
@@ -272,9 +280,6 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
                          tc::desc_at(mDS, pbo + kk * 2048), id_dqt, kk > 0 ? 1u : 0u);
           } else if ((t & 1) || t == n_iter - 1) {
             // dQ for the pair (2p, 2p+1): both dS^T buffers as one M = 128 operand
-            const int p = t >> 1;
-            if (p > 0 && !tc::mbar_wait(dq_free, (p - 1) & 1, abort)) break;
-            tc::tc_fence_after();
 #pragma unroll
             for (int kk = 0; kk < BK / 16; ++kk)
               tc::mma_ss(t_dqp, tc::desc_at(mDSpair, kk * 2048), tc::desc_at(mK, kk * 2048),
