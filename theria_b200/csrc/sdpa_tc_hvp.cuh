@@ -196,6 +196,12 @@ hvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
           const int st = t % ST;
           const uint32_t bo = (kPair ? (t & 1) : 0) * C::kP;  // dS/dSd buffer offset
           const uint32_t qo = st * 3 * C::kQ, to = qo + C::kQ, wo = qo + 2 * C::kQ;
+          // D = 64: the pair-hQ buffer wait comes before the P wait (a wait
+          // costs this MMA-issuing thread a few hundred cycles even when
+          // satisfied; here it overlaps the compute warps' work)
+          if (kPair && ((t & 1) || t == n_iter - 1) && (t >> 1) > 0 &&
+              !tc::mbar_wait(hq_free, ((t >> 1) - 1) & 1, abort))
+            break;
           if (!tc::mbar_wait(p_full, t & 1, abort)) break;
           tc::tc_fence_after();
 #pragma unroll
@@ -220,10 +226,7 @@ hvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
               tc::mma_ss(tmem, tc::desc_at(mTK, o), tc::desc_at(mDS, bo + o), id_hqt, 1u);
             }
           } else if ((t & 1) || t == n_iter - 1) {
-            // hQ = dSd K + dS tK for the pair (2p, 2p+1)
-            const int p = t >> 1;
-            if (p > 0 && !tc::mbar_wait(hq_free, (p - 1) & 1, abort)) break;
-            tc::tc_fence_after();
+            // hQ = dSd K + dS tK for the pair (2p, 2p+1) (buffer free: above)
 #pragma unroll
             for (int kk = 0; kk < BK / 16; ++kk) {
               const uint32_t o = kk * 2048;
