@@ -49,7 +49,10 @@ class MetaStep:
         self.fo = fo
         self.world = world
         self.params = [p for p in model.parameters()]
-        self.opt = torch.optim.Adam(self.params, lr=outer_lr, capturable=capturable)
+        # one fused kernel per step on the GPU (foreach kernels elsewhere)
+        fused = self.params[0].is_cuda
+        self.opt = torch.optim.Adam(self.params, lr=outer_lr, capturable=capturable,
+                                    fused=fused or None)
         n = sum(p.numel() for p in self.params)
         self.bucket = torch.zeros(n, dtype=torch.float32, device=self.params[0].device)
 
@@ -59,11 +62,7 @@ class MetaStep:
                                  inner_steps=self.inner_steps, fo=self.fo,
                                  reduction="sum", denom=self.meta_batch)
         grads = torch.autograd.grad(loss, self.params)
-        off = 0
-        for g in grads:
-            n = g.numel()
-            self.bucket[off:off + n].copy_(g.reshape(-1))
-            off += n
+        torch.cat([g.reshape(-1) for g in grads], out=self.bucket)  # one copy kernel
         return loss.detach()
 
     def exchange(self) -> None:
