@@ -14,8 +14,11 @@
 // stores the row terms c, z = rowsum(W OP), zdot = rowsum(W Odot).
 // Key tile BN = 128 for D = 64 and 64 for D = 128, so that
 // TMEM = S (BN) + Sd (BN) + OA (D) + [OP|OT] (2D) fits in 512 columns.
-// Warp roles: 0 TMA, 1 MMA issuer + TMEM owner, 2..9 compute (two groups
-// splitting each tile's key columns, four TMEM lane quarters each).
+// Warp roles: 0 TMA for Q/tQ and the K/tK ring (2 stages), 1 issues the S
+// and Sd' products and owns TMEM, 2 issues the PV products, 3 TMA for V/tV,
+// 4..11 compute (two groups splitting each tile's key columns, four TMEM
+// lane quarters each).  With S and PV on separate issuing threads, S(j+1)
+// runs on the tensor core while the CUDA cores still work on tile j.
 #pragma once
 
 #include "tc_common.cuh"
@@ -25,7 +28,9 @@ namespace tcjvp {
 
 constexpr int BM = 128;
 constexpr int NCOMPUTE = 256;
-constexpr int NTHREADS = 64 + NCOMPUTE;
+constexpr int NTHREADS = 128 + NCOMPUTE;
+constexpr int kFirstCompute = 4;
+constexpr int KST = 2;  // K/tK ring depth
 
 template <int HD>
 struct Cfg {
@@ -35,17 +40,17 @@ struct Cfg {
   static constexpr int kP = BM * BN * 2;
   static constexpr int oQ = 0;
   static constexpr int oTQ = oQ + kQ;
-  static constexpr int oK = oTQ + kQ;
+  static constexpr int oK = oTQ + kQ;         // stage s: K at oK + 2s*kKV, tK after it
   static constexpr int oTK = oK + kKV;
-  static constexpr int oV = oTK + kKV;
+  static constexpr int oV = oK + KST * 2 * kKV;
   static constexpr int oTV = oV + kKV;  // directly after V: [V | tV] is one B operand
   static constexpr int oP = oTV + kKV;
   static constexpr int oU = oP + kP;
   static constexpr int oStat = oU + kP;  // 3 x 128 floats: c, z, zdot partial sums
   static constexpr int oBar = oStat + 3 * BM * 4;
   // q_full, kt_full, kt_empty, vt_full, vt_empty, s_full, s_free, p_full,
-  // pv_done, c_ready, w_ready, drain
-  static constexpr int nBar = 12;
+  // pv_done, c_ready, w_ready, drain, kt_full[1], kt_empty[1], drain[1]
+  static constexpr int nBar = 15;
   static constexpr int oTmem = oBar + nBar * 8;
   static constexpr int oAbort = oTmem + 4;
   static constexpr int kAlloc = oAbort + 4 + 1024;
@@ -70,6 +75,10 @@ jvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
   uint64_t *q_full = bars, *kt_full = bars + 1, *kt_empty = bars + 2, *vt_full = bars + 3,
            *vt_empty = bars + 4, *s_full = bars + 5, *s_free = bars + 6, *p_full = bars + 7,
            *pv_done = bars + 8, *c_ready = bars + 9, *w_ready = bars + 10, *drain = bars + 11;
+  // second K/tK stage and the second issuer's drain
+  auto kt_full_s = [&](int st) { return st == 0 ? kt_full : bars + 12; };
+  auto kt_empty_s = [&](int st) { return st == 0 ? kt_empty : bars + 13; };
+  uint64_t* drain_b = bars + 14;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::oTmem);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + C::oAbort);
   float* stat_s = reinterpret_cast<float*>(smem + C::oStat);
@@ -98,7 +107,7 @@ jvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // ------------------------------------------------------------ producer
+    // ------------------------------------------------------------ producer: Q/tQ, K/tK
     if (lane == 0) {
       tc::mbar_expect_tx(q_full, 2 * C::kQ);
       for (int cb = 0; cb < HD / 64; ++cb) {
@@ -107,13 +116,27 @@ jvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       }
       int issued = 0;
       for (int j = 0; j < n_tiles; ++j) {
-        if (j >= 1 && !tc::mbar_wait(kt_empty, (j - 1) & 1, abort)) break;
-        tc::mbar_expect_tx(kt_full, 2 * C::kKV);
+        const int st = j % KST;
+        if (j >= KST && !tc::mbar_wait(kt_empty_s(st), ((j / KST) - 1) & 1, abort)) break;
+        uint8_t* base = smem + C::oK + st * 2 * C::kKV;
+        tc::mbar_expect_tx(kt_full_s(st), 2 * C::kKV);
         for (int cb = 0; cb < HD / 64; ++cb) {
-          tc::tma_load_3d(smem + C::oK + cb * BN * 128, &tm_k, kt_full, cb * 64, j * BN, bh);
-          tc::tma_load_3d(smem + C::oTK + cb * BN * 128, &tm_tk, kt_full, cb * 64, j * BN, bh);
+          tc::tma_load_3d(base + cb * BN * 128, &tm_k, kt_full_s(st), cb * 64, j * BN, bh);
+          tc::tma_load_3d(base + C::kKV + cb * BN * 128, &tm_tk, kt_full_s(st), cb * 64, j * BN,
+                          bh);
         }
-        if (j >= 1 && !tc::mbar_wait(vt_empty, (j - 1) & 1, abort)) { issued = -(j + 1); break; }
+        issued = j + 1;
+      }
+      tc::mbar_wait_drain(q_full, 0);
+      for (int j = issued > KST ? issued - KST : 0; j < issued; ++j)
+        tc::mbar_wait_drain(kt_full_s(j % KST), (j / KST) & 1);
+    }
+  } else if (warp == 3) {
+    // ------------------------------------------------------------ producer: V/tV
+    if (lane == 0) {
+      int issued = 0;
+      for (int j = 0; j < n_tiles; ++j) {
+        if (j >= 1 && !tc::mbar_wait(vt_empty, (j - 1) & 1, abort)) break;
         tc::mbar_expect_tx(vt_full, 2 * C::kKV);
         for (int cb = 0; cb < HD / 64; ++cb) {
           tc::tma_load_3d(smem + C::oV + cb * BN * 128, &tm_v, vt_full, cb * 64, j * BN, bh);
@@ -121,16 +144,10 @@ jvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
         }
         issued = j + 1;
       }
-      tc::mbar_wait_drain(q_full, 0);
-      if (issued > 0) {
-        tc::mbar_wait_drain(kt_full, (issued - 1) & 1);
-        tc::mbar_wait_drain(vt_full, (issued - 1) & 1);
-      } else if (issued < 0) {  // K/tK of tile -issued-1 went out, V/tV did not
-        tc::mbar_wait_drain(kt_full, (-issued - 1) & 1);
-      }
+      if (issued > 0) tc::mbar_wait_drain(vt_full, (issued - 1) & 1);
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
+  } else if (warp == 1 || warp == 2) {
+    // ------------------------------------------------------------ MMA issuers
     if (lane == 0) {
       constexpr int ab = tc::AbFmt<T>::v;
       constexpr uint32_t id_s = tc::idesc_f16(BM, BN, ab, 0, 0);
@@ -146,42 +163,54 @@ jvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       const uint64_t kP = tc::sw128_desc(a_p, 16, 1024), kU = tc::sw128_desc(a_u, 16, 1024);
       const uint64_t mV = tc::sw128_desc(a_v, BN * 128, 1024);
       bool ok = tc::mbar_wait(q_full, 0, abort);
-      for (int j = 0; ok && j < n_tiles; ++j) {
-        if (!tc::mbar_wait(kt_full, j & 1, abort)) break;
-        if (j >= 1 && !tc::mbar_wait(s_free, (j - 1) & 1, abort)) break;
-        tc::tc_fence_after();
+      if (warp == 1) {
+        // S = Q K^T and Sd' = tQ K^T + Q tK^T into the single S/Sd buffer,
+        // free once the compute warps loaded the previous tile's.
+        for (int j = 0; ok && j < n_tiles; ++j) {
+          const int st = j % KST;
+          if (!tc::mbar_wait(kt_full_s(st), (j / KST) & 1, abort)) break;
+          if (j >= 1 && !tc::mbar_wait(s_free, (j - 1) & 1, abort)) break;
+          tc::tc_fence_after();
+          const uint32_t so = st * 2 * C::kKV;  // K/tK stage offset
 #pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t oq = (kk / 4) * (BM * 128) + (kk % 4) * 32;
-          const uint32_t ok_ = (kk / 4) * (BN * 128) + (kk % 4) * 32;
-          const uint32_t acc = kk > 0 ? 1u : 0u;
-          tc::mma_ss(tmem + C::tS, tc::desc_at(kQ, oq), tc::desc_at(kK, ok_), id_s, acc);
-          tc::mma_ss(tmem + C::tSd, tc::desc_at(kTQ, oq), tc::desc_at(kK, ok_), id_s, acc);
-          tc::mma_ss(tmem + C::tSd, tc::desc_at(kQ, oq), tc::desc_at(kTK, ok_), id_s, 1u);
+          for (int kk = 0; kk < HD / 16; ++kk) {
+            const uint32_t oq = (kk / 4) * (BM * 128) + (kk % 4) * 32;
+            const uint32_t ok_ = so + (kk / 4) * (BN * 128) + (kk % 4) * 32;
+            const uint32_t acc = kk > 0 ? 1u : 0u;
+            tc::mma_ss(tmem + C::tS, tc::desc_at(kQ, oq), tc::desc_at(kK, ok_), id_s, acc);
+            tc::mma_ss(tmem + C::tSd, tc::desc_at(kTQ, oq), tc::desc_at(kK, ok_), id_s, acc);
+            tc::mma_ss(tmem + C::tSd, tc::desc_at(kQ, oq), tc::desc_at(kTK, ok_), id_s, 1u);
+          }
+          tc::mma_commit(s_full);
+          tc::mma_commit(kt_empty_s(st));
         }
-        tc::mma_commit(s_full);
-        tc::mma_commit(kt_empty);
-        if (!tc::mbar_wait(p_full, j & 1, abort)) break;
-        if (!tc::mbar_wait(vt_full, j & 1, abort)) break;
-        tc::tc_fence_after();
+        tc::mma_commit(drain);
+        tc::mbar_wait_drain(drain, 0);
+      } else {
+        // OA += U V and [OP | OT] += P [V | tV] (one N = 2D product)
+        for (int j = 0; ok && j < n_tiles; ++j) {
+          if (!tc::mbar_wait(vt_full, j & 1, abort)) break;  // operands before P
+          if (!tc::mbar_wait(p_full, j & 1, abort)) break;
+          tc::tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint32_t oa = (kk / 4) * (BM * 128) + (kk % 4) * 32;
-          const uint32_t ob = kk * 16 * 128;
-          const uint32_t acc = (j > 0 || kk > 0) ? 1u : 0u;
-          tc::mma_ss(tmem + C::tOA, tc::desc_at(kU, oa), tc::desc_at(mV, ob), id_a, acc);
-          tc::mma_ss(tmem + C::tOP, tc::desc_at(kP, oa), tc::desc_at(mV, ob), id_pt, acc);
+          for (int kk = 0; kk < BN / 16; ++kk) {
+            const uint32_t oa = (kk / 4) * (BM * 128) + (kk % 4) * 32;
+            const uint32_t ob = kk * 16 * 128;
+            const uint32_t acc = (j > 0 || kk > 0) ? 1u : 0u;
+            tc::mma_ss(tmem + C::tOA, tc::desc_at(kU, oa), tc::desc_at(mV, ob), id_a, acc);
+            tc::mma_ss(tmem + C::tOP, tc::desc_at(kP, oa), tc::desc_at(mV, ob), id_pt, acc);
+          }
+          tc::mma_commit(pv_done);
+          tc::mma_commit(vt_empty);
         }
-        tc::mma_commit(pv_done);
-        tc::mma_commit(vt_empty);
+        tc::mma_commit(drain_b);
+        tc::mbar_wait_drain(drain_b, 0);
       }
-      tc::mma_commit(drain);
-      tc::mbar_wait_drain(drain, 0);
     }
   } else {
     // ------------------------------------------------------------ compute
     constexpr int HALF = BN / 2;  // key columns per group
-    const int grp = (warp - 2) >> 2;
+    const int grp = (warp - kFirstCompute) >> 2;
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;  // TMEM lane = query row in tile
     const int row = q0 + r;
