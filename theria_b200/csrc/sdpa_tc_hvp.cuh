@@ -366,17 +366,21 @@ hvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       if (!wait(mma2_done + (t & 1), (t >> 1) & 1)) break;
       tc::tc_fence_after();
       if constexpr (!kPair) {
+        // hQ^T of tile t sits in the S^T columns, which the next tile's
+        // S-group waits for: read it out, release the columns, then add it.
         const int qb = (i_begin + t) * BQ;
-#pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
-          float v[32];
-          tc::tmem_ld32(tmem + lane_off + c * 32, v);
+        float v0[32], v1[32];
+        tc::tmem_ld32(tmem + lane_off, v0);
+        tc::tmem_ld32(tmem + lane_off + 32, v1);
+        tc::tc_fence_before();
+        tc::mbar_arrive(hq_free);
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int q = qb + c * 32 + e;
-            if (q < Tq) atomicAdd(hq_acc + (row_base + q) * HD + r, v[e] * scale);
-          }
+        for (int e = 0; e < 32; ++e) {
+          const int q = qb + e;
+          if (q < Tq) atomicAdd(hq_acc + (row_base + q) * HD + r, v0[e] * scale);
+          if (q + 32 < Tq) atomicAdd(hq_acc + (row_base + q + 32) * HD + r, v1[e] * scale);
         }
+        continue;
       } else {
         // hQ of the pair ending at tile t (lane = query row, 64 head dims):
         // read out of TMEM, release the buffer, stage it scaled in two
