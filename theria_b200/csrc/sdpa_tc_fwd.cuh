@@ -76,8 +76,10 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
   volatile int* abort = reinterpret_cast<volatile int*>(smem + L::oAbort);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bh = blockIdx.y;
-  const int cta = CAUSAL ? (gridDim.x - 1 - blockIdx.x) : blockIdx.x;  // heavy CTAs first
+  // Causal grids put the head index in x so the heaviest tiles of every head
+  // are dispatched first (longest-first over the whole grid).
+  const int bh = CAUSAL ? blockIdx.x : blockIdx.y;
+  const int cta = CAUSAL ? (gridDim.y - 1 - blockIdx.y) : blockIdx.x;
   const int q0 = cta * (NQT * BM);
   int n_tiles = (M + BN - 1) / BN;
   if (CAUSAL) n_tiles = min(n_tiles, (q0 + NQT * BM - 1) / BN + 1);

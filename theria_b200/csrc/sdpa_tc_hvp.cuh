@@ -80,8 +80,10 @@ hvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
   volatile int* abort = reinterpret_cast<volatile int*>(smem + C::oAbort);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bh = blockIdx.y;
-  const int k0 = blockIdx.x * BK;
+  // Causal grids put the head index in x so the heaviest tiles of every head
+  // are dispatched first (longest-first over the whole grid).
+  const int bh = CAUSAL ? blockIdx.x : blockIdx.y;
+  const int k0 = (CAUSAL ? blockIdx.y : blockIdx.x) * BK;
   const int n_qt = (Tq + BQ - 1) / BQ;
   const int i_begin = CAUSAL ? k0 / BQ : 0;
   const int n_iter = n_qt > i_begin ? n_qt - i_begin : 0;

@@ -247,6 +247,7 @@ int tc_fwd_launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMa
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   dim3 grid((unsigned)((s.T + tcfwd::NQT * tcfwd::BM - 1) / (tcfwd::NQT * tcfwd::BM)),
             (unsigned)(s.B * s.H));
+  if (CAUSAL) grid = dim3(grid.y, grid.x);  // head index in x: longest tiles first
   kern<<<grid, tcfwd::NTHREADS, smem, st>>>(mq, mk, mv, o, out_f32, lse, (int)s.T, (int)s.M,
                                             s.scale * 1.4426950408889634f);
   return launch_status();
@@ -285,6 +286,7 @@ int tc_bwd_launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMa
   constexpr int smem = tcbwd::Smem<HD>::kAlloc;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   dim3 grid((unsigned)((s.M + tcbwd::BK - 1) / tcbwd::BK), (unsigned)(s.B * s.H));
+  if (CAUSAL) grid = dim3(grid.y, grid.x);  // head index in x: longest tiles first
   kern<<<grid, tcbwd::NTHREADS, smem, st>>>(mq, mk, mv, mdo, mdq, lse, z, dq_acc, (T*)dk, (T*)dv,
                                             (int)s.T, (int)s.M, s.scale,
                                             s.scale * 1.4426950408889634f);
@@ -347,6 +349,7 @@ int tc_jvp_launch(const CUtensorMap* m, const float* lse, const void* w, void* o
   auto kern = tcjvp::jvp_kernel<T, HD, CAUSAL, W>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kAlloc);
   dim3 grid((unsigned)((s.T + tcjvp::BM - 1) / tcjvp::BM), (unsigned)(s.B * s.H));
+  if (CAUSAL) grid = dim3(grid.y, grid.x);  // head index in x: longest tiles first
   kern<<<grid, tcjvp::NTHREADS, C::kAlloc, st>>>(m[0], m[1], m[2], m[3], m[4], m[5], lse,
                                                  (const T*)w, (T*)o_tan, stats,
                                                  s.B * s.H * s.T, (int)s.T, (int)s.M, s.scale,
@@ -391,6 +394,7 @@ int tc_hvp_launch(const CUtensorMap* m, const float* lse, const float* stats, fl
   auto kern = tchvp::hvp_kernel<T, HD, CAUSAL>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kAlloc);
   dim3 grid((unsigned)((s.M + tchvp::BK - 1) / tchvp::BK), (unsigned)(s.B * s.H));
+  if (CAUSAL) grid = dim3(grid.y, grid.x);  // head index in x: longest tiles first
   kern<<<grid, tchvp::NTHREADS, C::kAlloc, st>>>(m[0], m[1], m[2], m[3], m[4], m[5], m[6], m[7],
                                                  lse,
                                                  stats, s.B * s.H * s.T, hq_acc, (T*)hk,
