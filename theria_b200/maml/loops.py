@@ -88,6 +88,9 @@ def _task_losses(logits, y):
                            reduction="none").view(nt, n).mean(dim=1)
 
 
+_ALIGN = 32  # floats: parameter alignment inside the flat fast weights
+
+
 def meta_loss_batched(model: nn.Module, tasks: TaskBatch, *, inner_lr: float = 0.1,
                       inner_steps: int = 1, fo: bool = False, reduction: str = "mean",
                       denom: int | None = None):
@@ -107,12 +110,22 @@ def meta_loss_batched(model: nn.Module, tasks: TaskBatch, *, inner_lr: float = 0
     params = [p for _, p in model.named_parameters()]
     shapes = [p.shape for p in params]
     sizes = [p.numel() for p in params]
-    theta = torch.cat([p.reshape(-1) for p in params])
+    # Every parameter starts on a 128-byte boundary of phi's rows (zero
+    # padding between them): with an odd row length the per-task views are
+    # misaligned and every GEMM and elementwise kernel on them falls back to
+    # its unvectorised, 1-element-aligned variant (several times slower).
+    padded = [-(-n // _ALIGN) * _ALIGN for n in sizes]
+    parts = []
+    for p, n, m in zip(params, sizes, padded):
+        parts.append(p.reshape(-1))
+        if m > n:
+            parts.append(p.new_zeros(m - n))
+    theta = torch.cat(parts)
     phi = theta.unsqueeze(0).expand(nt, theta.numel())
 
     def views(flat):
-        return OrderedDict((n, c.view(nt, *shp))
-                           for n, c, shp in zip(names, flat.split(sizes, dim=1), shapes))
+        return OrderedDict((n, c[:, :k].view(nt, *shp)) for n, c, k, shp in
+                           zip(names, flat.split(padded, dim=1), sizes, shapes))
 
     for _ in range(inner_steps):
         ls = _task_losses(model.forward_tasks(views(phi), tasks.x_s), tasks.y_s).sum()

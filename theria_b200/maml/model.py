@@ -89,8 +89,11 @@ class MAMLClassifier(nn.Module):
         nt, n, L = x.shape
         D, H = cfg.d_model, cfg.n_heads
         Dh = D // H
-        tok = params["tok"]
-        h = tok[torch.arange(nt, device=x.device).view(nt, 1, 1), x]  # (nt, n, L, D)
+        # Token embedding as a one-hot product: its gradient (and the
+        # gradient's gradient) is then a batched GEMM, not a sort-based
+        # scatter-add; exact in fp32 (one nonzero term per output).
+        onehot = F.one_hot(x.reshape(nt, n * L), cfg.vocab).to(params["tok"].dtype)
+        h = torch.bmm(onehot, params["tok"]).view(nt, n, L, D)
         h = h + params["pos"][:, :L].unsqueeze(1)
         for i in range(cfg.n_layers):
             p = lambda s: params[f"blocks.{i}.{s}"]  # noqa: E731
