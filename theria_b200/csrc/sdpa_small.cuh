@@ -8,10 +8,9 @@
 // classifier (N = 64, head dim 16, thousands of heads per call), where the
 // tiled kernels would run one nearly empty tile per head.
 //
-// Every product is an element-parallel loop over the output (thread e
-// computes elements e, e + blockDim, ...) with the reduction dimension read
-// from padded shared rows (stride D+1 or M+1); row statistics are one
-// thread per row.  Results are deterministic.
+// Every product is a register-blocked loop over the output (4 x 4 outputs
+// per thread, reduction read from padded shared rows of stride D+1 or M+1);
+// row statistics take one warp per row.  Results are deterministic.
 #pragma once
 
 #include "common.cuh"
@@ -56,48 +55,96 @@ __device__ __forceinline__ void load_mat(A* dst, const T* __restrict__ src, int 
   }
 }
 
-// The products below give each thread 2 x 2 blocks of outputs, so every
-// shared-memory value loaded feeds two FMAs (the single-output form was
-// bound by shared-memory loads).  Odd extents are handled by clamping the
-// second row/column to the first and not storing it.
+// Every product below is one generic block-wide kernel:
+//   out(r, c) = alpha * sum_k [A1(r,k) B1(c,k) + A2(r,k) B2(c,k)]
+// with A(r, k) = A[r*ar + k*ak] and B(c, k) = B[c*bc + k*bk] in shared memory.
+// Each thread owns a 4 x 4 block of outputs, so every value it loads feeds
+// four FMAs (shared-memory load bandwidth is the limit at these sizes), and
+// when the output is too small to occupy the block the reduction over k is
+// split over KS neighbouring lanes (k = ks, ks + KS, ...) and summed with
+// shuffles.  The lane layout keeps the loads free of bank conflicts for the
+// padded strides used here (D+1 for [rows][D], M+1 for score rows): the
+// rows of the two row groups sharing a warp are 4 apart, and columns are
+// blocked (c = 4 ct + n) when at most 8 column groups exist, interleaved
+// (c = ct + CT n) otherwise.
+constexpr int PB = 4;  // outputs per thread along rows and along columns
 
-// C[i][j] = alpha * (sum_d A1[i][d] B1[j][d] [+ A2[i][d] B2[j][d]])
+template <bool TWO, typename A, typename Store>
+__device__ __forceinline__ void prod(int R, int C, int K, const A* A1, const A* B1,
+                                     const A* A2, const A* B2, int ar, int ak, int bc,
+                                     int bk, A alpha, Store store) {
+  const int RT = (R + PB - 1) / PB, CT = (C + PB - 1) / PB;
+  int KS = 1;
+  while (KS < 8 && 2 * KS <= K && RT * CT * KS * 2 <= NTHREADS) KS *= 2;
+  const int t = threadIdx.x;
+  if (t >= RT * CT * KS) return;  // whole KS-lane groups drop out together
+  const int ks = t & (KS - 1), u = t / KS;
+  const int ct = u % CT;
+  int rt = u / CT;
+  if ((RT & 7) == 0) rt = (rt & ~7) | ((rt & 1) << 2) | ((rt >> 1) & 3);
+  const bool blocked = CT <= 8;
+  int ro[PB], co[PB];
+  bool rv[PB], cv[PB];
+#pragma unroll
+  for (int m = 0; m < PB; ++m) {
+    const int r = rt + RT * m;
+    rv[m] = r < R;
+    ro[m] = (rv[m] ? r : R - 1) * ar;
+    const int c = blocked ? ct * PB + m : ct + CT * m;
+    cv[m] = c < C;
+    co[m] = (cv[m] ? c : C - 1) * bc;
+  }
+  A acc[PB][PB];
+#pragma unroll
+  for (int m = 0; m < PB; ++m)
+#pragma unroll
+    for (int n = 0; n < PB; ++n) acc[m][n] = A(0);
+  // k = ks + KS * kk: with compile-time sizes (the specialised kernels) the
+  // loop unrolls fully and every load is a base pointer plus an immediate.
+  const int KQ = K / KS;
+  auto step = [&](const A* x, const A* y) {
+    A a[PB], b[PB];
+#pragma unroll
+    for (int m = 0; m < PB; ++m) a[m] = x[ro[m]];
+#pragma unroll
+    for (int n = 0; n < PB; ++n) b[n] = y[co[n]];
+#pragma unroll
+    for (int m = 0; m < PB; ++m)
+#pragma unroll
+      for (int n = 0; n < PB; ++n) acc[m][n] = fmaA(a[m], b[n], acc[m][n]);
+  };
+#pragma unroll
+  for (int term = 0; term < (TWO ? 2 : 1); ++term) {
+    const A* X = (term ? A2 : A1) + ks * ak;
+    const A* Y = (term ? B2 : B1) + ks * bk;
+#pragma unroll 4
+    for (int kk = 0; kk < KQ; ++kk) step(X + kk * KS * ak, Y + kk * KS * bk);
+    if (ks < K - KQ * KS) step(X + KQ * KS * ak, Y + KQ * KS * bk);
+  }
+  if (KS > 1) {
+    const int lane = threadIdx.x & 31;
+    const unsigned grp = (KS == 32 ? 0xffffffffu : ((1u << KS) - 1u) << (lane & ~(KS - 1)));
+    for (int o = KS >> 1; o > 0; o >>= 1)
+#pragma unroll
+      for (int m = 0; m < PB; ++m)
+#pragma unroll
+        for (int n = 0; n < PB; ++n) acc[m][n] += __shfl_xor_sync(grp, acc[m][n], o);
+  }
+#pragma unroll
+  for (int m = 0; m < PB; ++m)
+#pragma unroll
+    for (int n = 0; n < PB; ++n)
+      if (((m * PB + n) & (KS - 1)) == ks && rv[m] && cv[n])
+        store(rt + RT * m, blocked ? ct * PB + n : ct + CT * n, alpha * acc[m][n]);
+}
+
+// C[i][j] = alpha * (sum_d A1[i][d] B1[j][d] [+ A2[i][d] B2[j][d]])  (rows at stride D+1)
 template <bool TWO, typename A>
 __device__ __forceinline__ void abt_impl(A* C, int ldc, const A* A1, const A* B1,
                                          const A* A2, const A* B2, int rA, int rB,
                                          int D, A alpha) {
-  const int nbj = (rB + 1) >> 1, nb = ((rA + 1) >> 1) * nbj;
-  for (int e = threadIdx.x; e < nb; e += blockDim.x) {
-    const int i0 = 2 * (e / nbj), j0 = 2 * (e % nbj);
-    const int i1 = min(i0 + 1, rA - 1), j1 = min(j0 + 1, rB - 1);
-    A c00 = A(0), c01 = A(0), c10 = A(0), c11 = A(0);
-    {
-      const A *a0 = A1 + i0 * (D + 1), *a1 = A1 + i1 * (D + 1);
-      const A *b0 = B1 + j0 * (D + 1), *b1 = B1 + j1 * (D + 1);
-      for (int d = 0; d < D; ++d) {
-        c00 = fmaA(a0[d], b0[d], c00);
-        c01 = fmaA(a0[d], b1[d], c01);
-        c10 = fmaA(a1[d], b0[d], c10);
-        c11 = fmaA(a1[d], b1[d], c11);
-      }
-    }
-    if (TWO) {
-      const A *a0 = A2 + i0 * (D + 1), *a1 = A2 + i1 * (D + 1);
-      const A *b0 = B2 + j0 * (D + 1), *b1 = B2 + j1 * (D + 1);
-      for (int d = 0; d < D; ++d) {
-        c00 = fmaA(a0[d], b0[d], c00);
-        c01 = fmaA(a0[d], b1[d], c01);
-        c10 = fmaA(a1[d], b0[d], c10);
-        c11 = fmaA(a1[d], b1[d], c11);
-      }
-    }
-    C[i0 * ldc + j0] = alpha * c00;
-    if (j0 + 1 < rB) C[i0 * ldc + j0 + 1] = alpha * c01;
-    if (i0 + 1 < rA) {
-      C[(i0 + 1) * ldc + j0] = alpha * c10;
-      if (j0 + 1 < rB) C[(i0 + 1) * ldc + j0 + 1] = alpha * c11;
-    }
-  }
+  prod<TWO, A>(rA, rB, D, A1, B1, A2, B2, D + 1, 1, D + 1, 1, alpha,
+               [&](int i, int j, A x) { C[i * ldc + j] = x; });
 }
 
 template <typename A>
@@ -114,47 +161,14 @@ __device__ __forceinline__ void abt2(A* C, int ldc, const A* A1, const A* B1,
   abt_impl<true, A>(C, ldc, A1, B1, A2, B2, rA, rB, D, alpha);
 }
 
-template <typename OT, typename A>
-__device__ __forceinline__ void store2x2(OT* out, int ldo, int i0, int d0, int nI, int nD,
-                                         A alpha, A c00, A c01, A c10,
-                                         A c11) {
-  out[i0 * ldo + d0] = store_as<OT>(alpha * c00);
-  if (d0 + 1 < nD) out[i0 * ldo + d0 + 1] = store_as<OT>(alpha * c01);
-  if (i0 + 1 < nI) {
-    out[(i0 + 1) * ldo + d0] = store_as<OT>(alpha * c10);
-    if (d0 + 1 < nD) out[(i0 + 1) * ldo + d0 + 1] = store_as<OT>(alpha * c11);
-  }
-}
-
 // out[i][d] = alpha * sum_j (S1[i][j] X1[j][d] [+ S2[i][j] X2[j][d]])
-//   (S: [rS][cS] at stride lds; X: [cS][D]; out: [rS][D] dense)
+//   (S: [rS][cS] at stride lds; X: [cS][D] at stride D+1; out: [rS][D] dense)
 template <bool TWO, typename OT, typename A>
 __device__ __forceinline__ void sx_impl(OT* __restrict__ out, const A* S1, const A* X1,
                                         const A* S2, const A* X2, int lds, int rS,
                                         int cS, int D, A alpha) {
-  const int nbd = (D + 1) >> 1, nb = ((rS + 1) >> 1) * nbd;
-  for (int e = threadIdx.x; e < nb; e += blockDim.x) {
-    const int i0 = 2 * (e / nbd), d0 = 2 * (e % nbd);
-    const int i1 = min(i0 + 1, rS - 1), d1 = min(d0 + 1, D - 1);
-    A c00 = A(0), c01 = A(0), c10 = A(0), c11 = A(0);
-    for (int j = 0; j < cS; ++j) {
-      const A s0 = S1[i0 * lds + j], s1 = S1[i1 * lds + j];
-      const A x0 = X1[j * (D + 1) + d0], x1 = X1[j * (D + 1) + d1];
-      c00 = fmaA(s0, x0, c00);
-      c01 = fmaA(s0, x1, c01);
-      c10 = fmaA(s1, x0, c10);
-      c11 = fmaA(s1, x1, c11);
-      if (TWO) {
-        const A t0 = S2[i0 * lds + j], t1 = S2[i1 * lds + j];
-        const A y0 = X2[j * (D + 1) + d0], y1 = X2[j * (D + 1) + d1];
-        c00 = fmaA(t0, y0, c00);
-        c01 = fmaA(t0, y1, c01);
-        c10 = fmaA(t1, y0, c10);
-        c11 = fmaA(t1, y1, c11);
-      }
-    }
-    store2x2(out, D, i0, d0, rS, D, alpha, c00, c01, c10, c11);
-  }
+  prod<TWO, A>(rS, D, cS, S1, X1, S2, X2, lds, 1, 1, D + 1, alpha,
+               [&](int i, int d, A x) { out[i * D + d] = store_as<OT>(x); });
 }
 
 // out[j][d] = alpha * sum_i (S1[i][j] X1[i][d] [+ S2[i][j] X2[i][d]])  (S transposed)
@@ -162,29 +176,8 @@ template <bool TWO, typename OT, typename A>
 __device__ __forceinline__ void stx_impl(OT* __restrict__ out, const A* S1, const A* X1,
                                          const A* S2, const A* X2, int lds, int rS,
                                          int cS, int D, A alpha) {
-  const int nbd = (D + 1) >> 1, nb = ((cS + 1) >> 1) * nbd;
-  for (int e = threadIdx.x; e < nb; e += blockDim.x) {
-    const int j0 = 2 * (e / nbd), d0 = 2 * (e % nbd);
-    const int j1 = min(j0 + 1, cS - 1), d1 = min(d0 + 1, D - 1);
-    A c00 = A(0), c01 = A(0), c10 = A(0), c11 = A(0);
-    for (int i = 0; i < rS; ++i) {
-      const A s0 = S1[i * lds + j0], s1 = S1[i * lds + j1];
-      const A x0 = X1[i * (D + 1) + d0], x1 = X1[i * (D + 1) + d1];
-      c00 = fmaA(s0, x0, c00);
-      c01 = fmaA(s0, x1, c01);
-      c10 = fmaA(s1, x0, c10);
-      c11 = fmaA(s1, x1, c11);
-      if (TWO) {
-        const A t0 = S2[i * lds + j0], t1 = S2[i * lds + j1];
-        const A y0 = X2[i * (D + 1) + d0], y1 = X2[i * (D + 1) + d1];
-        c00 = fmaA(t0, y0, c00);
-        c01 = fmaA(t0, y1, c01);
-        c10 = fmaA(t1, y0, c10);
-        c11 = fmaA(t1, y1, c11);
-      }
-    }
-    store2x2(out, D, j0, d0, cS, D, alpha, c00, c01, c10, c11);
-  }
+  prod<TWO, A>(cS, D, rS, S1, X1, S2, X2, 1, lds, 1, D + 1, alpha,
+               [&](int j, int d, A x) { out[j * D + d] = store_as<OT>(x); });
 }
 
 template <typename OT, typename A>
@@ -211,6 +204,23 @@ __device__ __forceinline__ void stx2(OT* __restrict__ out, const A* S1, const A*
 }
 
 __device__ __forceinline__ bool masked(int i, int j, int causal) { return causal && j > i; }
+
+// Row passes run one warp per score row (lanes over the columns).
+template <typename A>
+__device__ __forceinline__ A warp_sum(A x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  return x;
+}
+template <typename A>
+__device__ __forceinline__ A warp_max(A x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x = maxA(x, __shfl_xor_sync(0xffffffffu, x, o));
+  return x;
+}
+#define THERIA_ROWS(i) \
+  for (int i = threadIdx.x >> 5; i < Tq; i += blockDim.x >> 5)
+#define THERIA_COLS(j) for (int j = threadIdx.x & 31; j < M; j += 32)
 
 // fp64 rebuilds the row logsumexp from the scores in double precision: the
 // float32 lse the forward saved would make P (and so every derivative) a
@@ -243,13 +253,15 @@ __device__ __forceinline__ void probs_from_lse(A* S, int lds, const A* lse_s, in
 }
 
 // ---------------------------------------------------------------- forward
-template <typename T, typename OT, typename A = float>
+template <typename T, typename OT, typename A = float, int NC = 0, int DC = 0>
 __global__ void __launch_bounds__(NTHREADS)
 fwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
            OT* __restrict__ o, float* __restrict__ lse, Shape s) {
   extern __shared__ __align__(16) unsigned char sm_raw[];
   A* sm = reinterpret_cast<A*>(sm_raw);
-  const int Tq = (int)s.T, M = (int)s.M, D = (int)s.D, lm = M + 1;
+  // NC, DC > 0: sequence lengths and head dim fixed at compile time
+  const int Tq = NC ? NC : (int)s.T, M = NC ? NC : (int)s.M, D = DC ? DC : (int)s.D;
+  const int lm = M + 1;
   const int64_t bh = blockIdx.x;
   A* Q = sm;
   A* K = Q + Tq * (D + 1);
@@ -261,33 +273,37 @@ fwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
   __syncthreads();
   abt(S, lm, Q, K, Tq, M, D, A(s.scale));
   __syncthreads();
-  for (int i = threadIdx.x; i < Tq; i += blockDim.x) {
+  THERIA_ROWS(i) {
+    A* row = S + i * lm;
     A m = -INFINITY;
-    for (int j = 0; j < M; ++j)
-      if (!masked(i, j, s.causal)) m = maxA(m, S[i * lm + j]);
+    THERIA_COLS(j) if (!masked(i, j, s.causal)) m = maxA(m, row[j]);
+    m = warp_max(m);
     A l = A(0);
-    for (int j = 0; j < M; ++j) {
-      const A p = masked(i, j, s.causal) ? A(0) : expA(S[i * lm + j] - m);
-      S[i * lm + j] = p;
+    THERIA_COLS(j) {
+      const A p = masked(i, j, s.causal) ? A(0) : expA(row[j] - m);
+      row[j] = p;
       l += p;
     }
+    l = warp_sum(l);
     const A inv = A(1) / l;
-    for (int j = 0; j < M; ++j) S[i * lm + j] *= inv;
-    if (lse) lse[bh * Tq + i] = m + logA(l);
+    THERIA_COLS(j) row[j] *= inv;
+    if (lse && (threadIdx.x & 31) == 0) lse[bh * Tq + i] = m + logA(l);
   }
   __syncthreads();
   sx(o + bh * Tq * D, S, lm, V, Tq, M, D, A(1));
 }
 
 // ---------------------------------------------------------------- backward
-template <typename T, typename A = float>
+template <typename T, typename A = float, int NC = 0, int DC = 0>
 __global__ void __launch_bounds__(NTHREADS)
 bwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
            const T* __restrict__ dout, const float* __restrict__ lse, T* __restrict__ dq,
            T* __restrict__ dk, T* __restrict__ dv, Shape s) {
   extern __shared__ __align__(16) unsigned char sm_raw[];
   A* sm = reinterpret_cast<A*>(sm_raw);
-  const int Tq = (int)s.T, M = (int)s.M, D = (int)s.D, lm = M + 1;
+  // NC, DC > 0: sequence lengths and head dim fixed at compile time
+  const int Tq = NC ? NC : (int)s.T, M = NC ? NC : (int)s.M, D = DC ? DC : (int)s.D;
+  const int lm = M + 1;
   const int64_t bh = blockIdx.x;
   A* Q = sm;
   A* G = Q + Tq * (D + 1);  // dO
@@ -309,10 +325,13 @@ bwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
   __syncthreads();
   probs_from_lse(P, lm, L, Tq, M, s.causal);
   __syncthreads();
-  for (int i = threadIdx.x; i < Tq; i += blockDim.x) {
+  THERIA_ROWS(i) {
+    const A* p = P + i * lm;
+    A* ds = DS + i * lm;
     A z = A(0);
-    for (int j = 0; j < M; ++j) z = fmaA(P[i * lm + j], DS[i * lm + j], z);
-    for (int j = 0; j < M; ++j) DS[i * lm + j] = P[i * lm + j] * (DS[i * lm + j] - z);
+    THERIA_COLS(j) z = fmaA(p[j], ds[j], z);
+    z = warp_sum(z);
+    THERIA_COLS(j) ds[j] = p[j] * (ds[j] - z);
   }
   __syncthreads();
   if (dq) sx(dq + bh * Tq * D, DS, lm, K, Tq, M, D, A(s.scale));
@@ -321,14 +340,16 @@ bwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
 }
 
 // ---------------------------------------------------------------- JVP
-template <typename T, typename A = float>
+template <typename T, typename A = float, int NC = 0, int DC = 0>
 __global__ void __launch_bounds__(NTHREADS)
 jvp_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
            const T* __restrict__ tq, const T* __restrict__ tk, const T* __restrict__ tv,
            const float* __restrict__ lse, T* __restrict__ o_tan, Shape s) {
   extern __shared__ __align__(16) unsigned char sm_raw[];
   A* sm = reinterpret_cast<A*>(sm_raw);
-  const int Tq = (int)s.T, M = (int)s.M, D = (int)s.D, lm = M + 1;
+  // NC, DC > 0: sequence lengths and head dim fixed at compile time
+  const int Tq = NC ? NC : (int)s.T, M = NC ? NC : (int)s.M, D = DC ? DC : (int)s.D;
+  const int lm = M + 1;
   const int64_t bh = blockIdx.x;
   A* Q = sm;
   A* TQ = Q + Tq * (D + 1);
@@ -354,10 +375,13 @@ jvp_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
   __syncthreads();
   probs_from_lse(P, lm, L, Tq, M, s.causal);
   __syncthreads();
-  for (int i = threadIdx.x; i < Tq; i += blockDim.x) {
+  THERIA_ROWS(i) {
+    const A* p = P + i * lm;
+    A* sd = SD + i * lm;
     A c = A(0);
-    for (int j = 0; j < M; ++j) c = fmaA(P[i * lm + j], SD[i * lm + j], c);
-    for (int j = 0; j < M; ++j) SD[i * lm + j] = P[i * lm + j] * (SD[i * lm + j] - c);
+    THERIA_COLS(j) c = fmaA(p[j], sd[j], c);
+    c = warp_sum(c);
+    THERIA_COLS(j) sd[j] = p[j] * (sd[j] - c);
   }
   __syncthreads();
   sx2(o_tan + bh * Tq * D, SD, V, P, TV, lm, Tq, M, D, A(1));
@@ -365,7 +389,7 @@ jvp_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
 
 // ---------------------------------------------------------------- HVP
 // Full HVP of L = <O, W> along (tQ, tK, tV): hQ, hK, hV and Odot.
-template <typename T, typename A = float>
+template <typename T, typename A = float, int NC = 0, int DC = 0>
 __global__ void __launch_bounds__(NTHREADS)
 hvp_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
            const T* __restrict__ w, const float* __restrict__ lse, const T* __restrict__ tq,
@@ -373,7 +397,9 @@ hvp_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
            T* __restrict__ hk, T* __restrict__ hv, T* __restrict__ o_tan, Shape s) {
   extern __shared__ __align__(16) unsigned char sm_raw[];
   A* sm = reinterpret_cast<A*>(sm_raw);
-  const int Tq = (int)s.T, M = (int)s.M, D = (int)s.D, lm = M + 1;
+  // NC, DC > 0: sequence lengths and head dim fixed at compile time
+  const int Tq = NC ? NC : (int)s.T, M = NC ? NC : (int)s.M, D = DC ? DC : (int)s.D;
+  const int lm = M + 1;
   const int64_t bh = blockIdx.x;
   const int qsz = Tq * (D + 1), ksz = M * (D + 1), ssz = Tq * lm;
   A* Q = sm;
@@ -407,22 +433,25 @@ hvp_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
   __syncthreads();
   probs_from_lse(P, lm, L, Tq, M, s.causal);
   __syncthreads();
-  for (int i = threadIdx.x; i < Tq; i += blockDim.x) {
+  THERIA_ROWS(i) {
     A* p = P + i * lm;
     A* pd = PD + i * lm;
     A* ds = DS + i * lm;
     A* dsd = DSD + i * lm;
     A c = A(0), z = A(0);
-    for (int j = 0; j < M; ++j) {
+    THERIA_COLS(j) {
       c = fmaA(p[j], pd[j], c);
       z = fmaA(p[j], ds[j], z);
     }
+    c = warp_sum(c);
+    z = warp_sum(z);
     A zd = A(0);
-    for (int j = 0; j < M; ++j) {
+    THERIA_COLS(j) {
       pd[j] = p[j] * (pd[j] - c);                 // Pdot
       zd = fmaA(pd[j], ds[j], fmaA(p[j], dsd[j], zd));  // rowsum(W Odot)
     }
-    for (int j = 0; j < M; ++j) {
+    zd = warp_sum(zd);
+    THERIA_COLS(j) {
       const A g = ds[j] - z;
       dsd[j] = pd[j] * g + p[j] * (dsd[j] - zd);  // dSdot
       ds[j] = p[j] * g;                           // dS
@@ -434,6 +463,9 @@ hvp_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
   if (hv) stx(hv + ko, PD, lm, W, Tq, M, D, A(1));
   if (o_tan) sx2(o_tan + qo, PD, V, P, TV, lm, Tq, M, D, A(1));
 }
+
+#undef THERIA_ROWS
+#undef THERIA_COLS
 
 }  // namespace small
 }  // namespace theria

@@ -177,6 +177,14 @@ bool f64_fits(const Shape& s, int n_q, int n_k, int n_s) {
          small::smem_bytes((int)s.T, (int)s.M, (int)s.D, n_q, n_k, n_s, sizeof(double)) <= kMaxSmem;
 }
 
+// The full-MAML head shape (T = M = 64, head dim 16, fp32) runs kernels
+// specialised at compile time; every other shape the generic ones.
+template <typename T, typename A>
+bool small_spec(const Shape& s) {
+  return std::is_same<T, float>::value && std::is_same<A, float>::value && s.T == 64 &&
+         s.M == 64 && s.D == 16;
+}
+
 template <typename K>
 void small_setup(K kern, size_t bytes) {
   if (bytes > 48 * 1024)
@@ -190,11 +198,15 @@ int small_fwd(const void* q, const void* k, const void* v, void* o, int o_dtype,
   const unsigned grid = (unsigned)(s.B * s.H);
   if (o_dtype == THERIA_F32) {
     auto kern = small::fwd_kernel<T, float, A>;
+    if constexpr (std::is_same<T, float>::value && std::is_same<A, float>::value)
+      if (small_spec<T, A>(s)) kern = small::fwd_kernel<T, float, A, 64, 16>;
     small_setup(kern, sm);
     kern<<<grid, small::NTHREADS, sm, st>>>((const T*)q, (const T*)k, (const T*)v, (float*)o,
                                             lse, s);
   } else {
     auto kern = small::fwd_kernel<T, T, A>;
+    if constexpr (std::is_same<T, float>::value && std::is_same<A, float>::value)
+      if (small_spec<T, A>(s)) kern = small::fwd_kernel<T, T, A, 64, 16>;
     small_setup(kern, sm);
     kern<<<grid, small::NTHREADS, sm, st>>>((const T*)q, (const T*)k, (const T*)v, (T*)o, lse,
                                             s);
@@ -207,6 +219,8 @@ int small_bwd(const void* q, const void* k, const void* v, const void* dout, con
               void* dq, void* dk, void* dv, const Shape& s, cudaStream_t st) {
   const size_t sm = small::smem_bytes((int)s.T, (int)s.M, (int)s.D, 2, 2, 2, sizeof(A));
   auto kern = small::bwd_kernel<T, A>;
+  if constexpr (std::is_same<T, float>::value && std::is_same<A, float>::value)
+    if (small_spec<T, A>(s)) kern = small::bwd_kernel<T, A, 64, 16>;
   small_setup(kern, sm);
   kern<<<(unsigned)(s.B * s.H), small::NTHREADS, sm, st>>>(
       (const T*)q, (const T*)k, (const T*)v, (const T*)dout, lse, (T*)dq, (T*)dk, (T*)dv, s);
@@ -218,6 +232,8 @@ int small_jvp(const void* q, const void* k, const void* v, const void* tq, const
               const void* tv, const float* lse, void* o_tan, const Shape& s, cudaStream_t st) {
   const size_t sm = small::smem_bytes((int)s.T, (int)s.M, (int)s.D, 2, 4, 2, sizeof(A));
   auto kern = small::jvp_kernel<T, A>;
+  if constexpr (std::is_same<T, float>::value && std::is_same<A, float>::value)
+    if (small_spec<T, A>(s)) kern = small::jvp_kernel<T, A, 64, 16>;
   small_setup(kern, sm);
   kern<<<(unsigned)(s.B * s.H), small::NTHREADS, sm, st>>>(
       (const T*)q, (const T*)k, (const T*)v, (const T*)tq, (const T*)tk, (const T*)tv, lse,
@@ -231,6 +247,8 @@ int small_hvp(const void* q, const void* k, const void* v, const void* w, const 
               void* o_tan, const Shape& s, cudaStream_t st) {
   const size_t sm = small::smem_bytes((int)s.T, (int)s.M, (int)s.D, 3, 4, 4, sizeof(A));
   auto kern = small::hvp_kernel<T, A>;
+  if constexpr (std::is_same<T, float>::value && std::is_same<A, float>::value)
+    if (small_spec<T, A>(s)) kern = small::hvp_kernel<T, A, 64, 16>;
   small_setup(kern, sm);
   kern<<<(unsigned)(s.B * s.H), small::NTHREADS, sm, st>>>(
       (const T*)q, (const T*)k, (const T*)v, (const T*)w, lse, (const T*)tq, (const T*)tk,
