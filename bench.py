@@ -538,15 +538,20 @@ def theria_arm(args, world, rank, local):
 
 def profile_case(case):
     """A few launches of one operator at a size ncu can capture in minutes
-    (inputs still larger than L2): --profile-case fwdbwd|jvp|hvp."""
+    (inputs still larger than L2): --profile-case fwdbwd|jvp|hvp, or
+    maml_heads: forward + HVP of 3,200 fp32 MAML heads [800, 4, 64, 16]
+    (the whole-head kernels)."""
     from theria_b200.attention import ops
     torch.cuda.set_device(0)
-    if case == "fwdbwd":
+    if case == "maml_heads":
+        shape = (800, 4, 64, 16)
+    elif case == "fwdbwd":
         shape = (1, 16, 4096, 128)
     else:
         shape = (CFG3["B"], CFG3["H"], CFG3["N"], CFG3["D"])
     gen = torch.Generator("cpu").manual_seed(0)
-    q, k, v, w, tq, tk, tv = (randn(shape, gen, torch.bfloat16, "cuda") for _ in range(7))
+    dt = torch.float32 if case == "maml_heads" else torch.bfloat16
+    q, k, v, w, tq, tk, tv = (randn(shape, gen, dt, "cuda") for _ in range(7))
     for _ in range(3):
         o, lse = ops.forward(q, k, v)
         if case == "fwdbwd":
@@ -571,7 +576,8 @@ def main():
                     help="add the configs[4] long-sequence causal sweep to `extra`")
     ap.add_argument("--cpu-budget", type=float, default=12.0,
                     help="seconds of CPU work for the cpu_baseline sample")
-    ap.add_argument("--profile-case", choices=["fwdbwd", "jvp", "hvp"], default=None,
+    ap.add_argument("--profile-case", choices=["fwdbwd", "jvp", "hvp", "maml_heads"],
+                    default=None,
                     help="run a few launches of one operator for ncu, print no bench line")
     args = ap.parse_args()
     if args.profile_case:

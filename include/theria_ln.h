@@ -1,0 +1,53 @@
+/*
+ * theria_ln.h -- C ABI of the task-batched LayerNorm used by the full-MAML
+ * model (libtheria_sm100.so), with its first and second derivatives.
+ *
+ * x, y, gy, gx, u, dx, dgy are [nt, R, D] float32, contiguous; w, b are
+ * [nt, D] float32 with row stride ldw (elements; 0 = one row shared by
+ * all tasks); gw, gb, a, c, dw are
+ * [nt, D] contiguous.  eps is added to the variance (as torch layer_norm).
+ *   forward      y  = (x - mean) * rstd * w + b
+ *   backward     gx = rstd * P(gy * w), gw = sum_rows gy * xhat, gb = sum_rows gy
+ *   backward of the backward, for cotangents (u, a, c) of (gx, gw, gb):
+ *                dx, dw, dgy   (u, a, c may be NULL: zero)
+ * where P(v) = v - mean(v) - xhat * mean(v * xhat).  The row sums go through
+ * a caller-owned workspace of theria_ln_workspace_bytes(nt, R, D) bytes and a
+ * second deterministic kernel.  Stream-ordered, no allocation, no host
+ * synchronisation; each call returns a THERIA_* status (theria_sdpa.h).
+ *
+ * The reference library has no LayerNorm of its own: its MAML loops
+ * (theria/maml/loops.py:42-123) run user models through torch autograd.
+ * These entry points serve this build's benchmark model, whose LayerNorm
+ * double backward would otherwise be dozens of small torch kernels.
+ */
+#ifndef THERIA_LN_H
+#define THERIA_LN_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* largest normalised dimension the kernels accept */
+#define THERIA_LN_MAX_D 256
+
+int64_t theria_ln_workspace_bytes(int64_t nt, int64_t R, int64_t D);
+
+int theria_ln_fwd(const float* x, const float* w, const float* b, int64_t ldw, float* y,
+                  int64_t nt, int64_t R, int64_t D, float eps, void* stream);
+
+int theria_ln_bwd(const float* x, const float* w, int64_t ldw, const float* gy, float* gx,
+                  float* gw, float* gb, void* workspace, int64_t workspace_bytes,
+                  int64_t nt, int64_t R, int64_t D, float eps, void* stream);
+
+int theria_ln_bwd2(const float* x, const float* w, int64_t ldw, const float* gy,
+                   const float* u, const float* a, const float* c, float* dx, float* dw,
+                   float* dgy, void* workspace, int64_t workspace_bytes, int64_t nt,
+                   int64_t R, int64_t D, float eps, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* THERIA_LN_H */

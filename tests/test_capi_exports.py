@@ -1,5 +1,5 @@
-"""The C-ABI library loads and exports every entry point include/theria_sdpa.h
-declares; host-only calls (status strings, workspace sizes, argument
+"""The C-ABI library loads and exports every entry point the headers in
+include/ declare; host-only calls (status strings, workspace sizes, argument
 rejection) behave.  No kernel is launched, so no GPU is needed."""
 
 import ctypes
@@ -10,18 +10,22 @@ import pytest
 
 from theria_b200 import _lib
 
-HEADER = os.path.join(os.path.dirname(__file__), "..", "include", "theria_sdpa.h")
+INCLUDE = os.path.join(os.path.dirname(__file__), "..", "include")
+HEADERS = sorted(os.path.join(INCLUDE, f) for f in os.listdir(INCLUDE) if f.endswith(".h"))
 
 
 def declared_functions():
-    src = open(HEADER).read()
-    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
-    return sorted(set(re.findall(r"\b(theria_\w+)\s*\(", src)))
+    names = set()
+    for h in HEADERS:
+        src = re.sub(r"/\*.*?\*/", "", open(h).read(), flags=re.S)
+        names.update(re.findall(r"\b(theria_\w+)\s*\(", src))
+    return sorted(names)
 
 
 def test_header_declares_the_entry_points():
     names = declared_functions()
-    for n in ("theria_sdpa_fwd", "theria_sdpa_bwd", "theria_sdpa_jvp", "theria_sdpa_hvp"):
+    for n in ("theria_sdpa_fwd", "theria_sdpa_bwd", "theria_sdpa_jvp", "theria_sdpa_hvp",
+              "theria_ln_fwd", "theria_ln_bwd", "theria_ln_bwd2"):
         assert n in names
 
 
@@ -84,3 +88,15 @@ def test_empty_problem_is_a_no_op():
     st = lib.theria_sdpa_fwd(None, None, None, None, 0, None, 0, 4, 4, 4, 16, 0, 0.25, 0,
                              None)
     assert st == _lib.THERIA_OK
+
+
+def test_layer_norm_arguments_checked_on_the_host():
+    lib = _lib.load()
+    p = ctypes.c_void_p(16)
+    assert lib.theria_ln_fwd(p, p, p, 512, p, 4, 100, 512, 1e-5, None) == \
+        _lib.THERIA_ERR_UNSUPPORTED
+    assert lib.theria_ln_fwd(p, p, p, 32, p, 4, 100, 64, 1e-5, None) == \
+        _lib.THERIA_ERR_INVALID_ARG  # ldw < D
+    assert lib.theria_ln_bwd(p, p, 64, p, p, p, p, None, 0, 4, 100, 64, 1e-5, None) == \
+        _lib.THERIA_ERR_WORKSPACE
+    assert lib.theria_ln_workspace_bytes(4, 100, 64) == 4 * 2 * 2 * 64 * 4

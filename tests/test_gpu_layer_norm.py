@@ -1,0 +1,77 @@
+"""Fused task-batched LayerNorm (include/theria_ln.h): forward, gradient and
+second derivative against the composed torch form in float64 on the CPU,
+with affine rows taken as strided views of a padded flat buffer (the MAML
+fast-weight layout) and head dims that do and do not fill the warp lanes."""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+if not torch.cuda.is_available():
+    pytest.skip("CUDA not available", allow_module_level=True)
+
+from theria_b200.maml.layer_norm import layer_norm, layer_norm_reference  # noqa: E402
+
+
+def _rel(a, b):
+    return ((a.double().cpu() - b).abs().max() / b.abs().max().clamp_min(1e-30)).item()
+
+
+def _inputs(nt, rows, D, seed):
+    g = torch.Generator("cpu").manual_seed(seed)
+    x = torch.randn(nt, *rows, D, generator=g) * 2 + 0.5
+    flat = torch.zeros(nt, 2 * D + 40)           # padded rows: stride != D
+    flat[:, :D] = 1 + 0.3 * torch.randn(nt, D, generator=g)
+    flat[:, D + 8:2 * D + 8] = torch.randn(nt, D, generator=g)
+    r = torch.randn(nt, *rows, D, generator=g)
+    vx = torch.randn(nt, *rows, D, generator=g)
+    vw, vb = torch.randn(nt, D, generator=g), torch.randn(nt, D, generator=g)
+    return x, flat, r, vx, vw, vb
+
+
+def _run(fn, x, flat, r, vx, vw, vb, D):
+    flat = flat.clone().requires_grad_(True)
+    w, b = flat[:, :D], flat[:, D + 8:2 * D + 8]
+    x = x.clone().requires_grad_(True)
+    r = r.clone().requires_grad_(True)
+    y = fn(x, w, b)
+    gx, gw, gb = torch.autograd.grad((y * r).sum(), (x, w, b), create_graph=True)
+    l2 = (gx * vx).sum() + (gw * vw).sum() + (gb * vb).sum()
+    dx, dflat, dr = torch.autograd.grad(l2, (x, flat, r))
+    return y, gx, gw, gb, dx, dflat[:, :D], dr
+
+
+@pytest.mark.parametrize("nt,rows,D", [(3, (5, 7), 64), (2, (130,), 48), (1, (3, 64), 100),
+                                       (4, (1,), 16)])
+def test_layer_norm_matches_composed_torch(nt, rows, D):
+    args = _inputs(nt, rows, D, seed=D)
+    ref = _run(layer_norm_reference, *(t.double() for t in args), D)
+    got = _run(layer_norm, *(t.cuda() for t in args), D)
+    names = ["y", "gx", "gw", "gb", "d2x", "d2w", "d2gy"]
+    for n, a, b in zip(names, got, ref):
+        tol = 1e-5 if n in ("y", "gx", "gw", "gb") else 1e-4
+        assert _rel(a, b) <= tol, (n, _rel(a, b))
+
+
+def test_layer_norm_second_derivative_without_some_cotangents():
+    # only gx is used downstream: the gw / gb cotangents arrive as None
+    x, flat, r, vx, _, _ = _inputs(2, (9,), 64, seed=3)
+
+    def run(fn, dev, dt):
+        xx = x.to(dev, dt).requires_grad_(True)
+        w = flat[:, :64].to(dev, dt).requires_grad_(True)
+        b = flat[:, 72:136].to(dev, dt)
+        y = fn(xx, w, b)
+        (gx,) = torch.autograd.grad((y * r.to(dev, dt)).sum(), (xx,), create_graph=True)
+        return torch.autograd.grad((gx * vx.to(dev, dt)).sum(), (xx, w))
+
+    for a, b in zip(run(layer_norm, "cuda", torch.float32),
+                    run(layer_norm_reference, "cpu", torch.float64)):
+        assert _rel(a, b) <= 1e-4
+
+
+def test_layer_norm_refuses_non_float32():
+    x = torch.randn(2, 4, 64, device="cuda", dtype=torch.float16)
+    w = torch.ones(2, 64, device="cuda", dtype=torch.float16)
+    with pytest.raises(ValueError):
+        layer_norm(x, w, w)

@@ -32,7 +32,8 @@ _i64 = ctypes.c_int64
 _i = ctypes.c_int
 _f = ctypes.c_float
 
-# name -> (restype, argtypes); must mirror include/theria_sdpa.h exactly.
+# name -> (restype, argtypes); must mirror include/theria_sdpa.h and
+# include/theria_ln.h exactly.
 SIGNATURES = {
     "theria_status_string": (ctypes.c_char_p, [_i]),
     "theria_version": (ctypes.c_char_p, []),
@@ -48,6 +49,12 @@ SIGNATURES = {
     "theria_sdpa_scores": (_i, [_vp, _vp, _vp, _i] + [_i64] * 5 + [_i, _f, _vp]),
     "theria_sdpa_probs": (_i, [_vp] * 4 + [_i64] * 5 + [_i, _f, _i, _vp]),
     "theria_launch_count": (_i64, []),
+    "theria_ln_workspace_bytes": (_i64, [_i64] * 3),
+    "theria_ln_fwd": (_i, [_vp, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _f, _vp]),
+    "theria_ln_bwd": (_i, [_vp, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _i64,
+                           _i64, _i64, _i64, _f, _vp]),
+    "theria_ln_bwd2": (_i, [_vp, _vp, _i64] + [_vp] * 7 + [_vp, _i64, _i64, _i64, _i64, _f,
+                                                         _vp]),
     "theria_get_device_error": (_i, [ctypes.POINTER(ctypes.c_int), _vp]),
     "theria_clear_device_error": (_i, [_vp]),
 }

@@ -14,6 +14,8 @@
 #include "sdpa_scores.cuh"
 #include "sdpa_simt.cuh"
 #include "sdpa_small.cuh"
+#include "maml_ln.cuh"
+#include "../../include/theria_ln.h"
 #include "sdpa_tc_bwd.cuh"
 #include "sdpa_tc_fwd.cuh"
 #include "sdpa_tc_jvp.cuh"
@@ -747,6 +749,111 @@ int theria_sdpa_bwd_noalloc(const void* q, const void* k, const void* v, const v
   return theria_sdpa_bwd(q, k, v, o, o_dtype, dout, lse, dq, dk, dv, scratch,
                          (int64_t)THERIA_NOALLOC_SCRATCH_BYTES, B, H, T, M, D, dtype, scale,
                          causal, stream);
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------ MAML LayerNorm
+namespace {
+int ln_check(int64_t nt, int64_t R, int64_t D, int64_t ldw) {
+  // ldw == 0: every task reads the same affine row (a broadcast view)
+  if (nt < 0 || R < 0 || D <= 0 || (ldw < D && ldw != 0)) return THERIA_ERR_INVALID_ARG;
+  if (D > THERIA_LN_MAX_D || nt > 65535) return THERIA_ERR_UNSUPPORTED;
+  return THERIA_OK;
+}
+int64_t ln_ctas(int64_t R) { return (R + ln::ROWS_PER_CTA - 1) / ln::ROWS_PER_CTA; }
+
+// V = values per lane: D <= 32 V.
+template <template <int> class F, typename... Args>
+int ln_dispatch(int64_t D, Args... args) {
+  if (D <= 32) return F<1>::run(args...);
+  if (D <= 64) return F<2>::run(args...);
+  if (D <= 128) return F<4>::run(args...);
+  return F<8>::run(args...);
+}
+
+template <int V>
+struct LnFwd {
+  static int run(const float* x, const float* w, const float* b, int64_t ldw, float* y,
+                 int64_t nt, int64_t R, int D, float eps, cudaStream_t st) {
+    dim3 grid((unsigned)ln_ctas(R), (unsigned)nt);
+    ln::fwd_kernel<V><<<grid, ln::WARPS * 32, 0, st>>>(x, w, b, ldw, y, R, D, eps);
+    return launch_status();
+  }
+};
+template <int V>
+struct LnBwd {
+  static int run(const float* x, const float* w, int64_t ldw, const float* gy, float* gx,
+                 float* gw, float* gb, float* ws, int64_t nt, int64_t R, int D, float eps,
+                 cudaStream_t st) {
+    dim3 grid((unsigned)ln_ctas(R), (unsigned)nt);
+    ln::bwd_kernel<V><<<grid, ln::WARPS * 32, 0, st>>>(x, w, ldw, gy, gx, ws, R, D, eps);
+    if (int e = launch_status()) return e;
+    ln::colsum_kernel<<<(unsigned)nt, 256, 0, st>>>(ws, gw, gb, (int)grid.x, 2, D);
+    return launch_status();
+  }
+};
+template <int V>
+struct LnBwd2 {
+  static int run(const float* x, const float* w, int64_t ldw, const float* gy, const float* u,
+                 const float* a, const float* c, float* dx, float* dw, float* dgy, float* ws,
+                 int64_t nt, int64_t R, int D, float eps, cudaStream_t st) {
+    dim3 grid((unsigned)ln_ctas(R), (unsigned)nt);
+    ln::bwd2_kernel<V><<<grid, ln::WARPS * 32, 0, st>>>(x, w, ldw, gy, u, a, c, dx, dgy, ws,
+                                                       R, D, eps);
+    if (int e = launch_status()) return e;
+    ln::colsum_kernel<<<(unsigned)nt, 256, 0, st>>>(ws, dw, dw, (int)grid.x, 1, D);
+    return launch_status();
+  }
+};
+}  // namespace
+
+extern "C" {
+
+int64_t theria_ln_workspace_bytes(int64_t nt, int64_t R, int64_t D) {
+  return nt * ln_ctas(R) * 2 * D * (int64_t)sizeof(float);
+}
+
+int theria_ln_fwd(const float* x, const float* w, const float* b, int64_t ldw, float* y,
+                  int64_t nt, int64_t R, int64_t D, float eps, void* stream) {
+  if (int e = ln_check(nt, R, D, ldw)) return e;
+  if (nt == 0 || R == 0) return THERIA_OK;
+  if (!x || !w || !b || !y) return THERIA_ERR_INVALID_ARG;
+  return ln_dispatch<LnFwd>(D, x, w, b, ldw, y, nt, R, (int)D, eps, (cudaStream_t)stream);
+}
+
+int theria_ln_bwd(const float* x, const float* w, int64_t ldw, const float* gy, float* gx,
+                  float* gw, float* gb, void* workspace, int64_t workspace_bytes,
+                  int64_t nt, int64_t R, int64_t D, float eps, void* stream) {
+  if (int e = ln_check(nt, R, D, ldw)) return e;
+  if (nt == 0) return THERIA_OK;
+  if (!x || !w || !gy || !gx || !gw || !gb) return THERIA_ERR_INVALID_ARG;
+  if (R == 0) {
+    cudaMemsetAsync(gw, 0, nt * D * sizeof(float), (cudaStream_t)stream);
+    cudaMemsetAsync(gb, 0, nt * D * sizeof(float), (cudaStream_t)stream);
+    return THERIA_OK;
+  }
+  if (!workspace || workspace_bytes < theria_ln_workspace_bytes(nt, R, D))
+    return THERIA_ERR_WORKSPACE;
+  return ln_dispatch<LnBwd>(D, x, w, ldw, gy, gx, gw, gb, (float*)workspace, nt, R, (int)D,
+                            eps, (cudaStream_t)stream);
+}
+
+int theria_ln_bwd2(const float* x, const float* w, int64_t ldw, const float* gy,
+                   const float* u, const float* a, const float* c, float* dx, float* dw,
+                   float* dgy, void* workspace, int64_t workspace_bytes, int64_t nt,
+                   int64_t R, int64_t D, float eps, void* stream) {
+  if (int e = ln_check(nt, R, D, ldw)) return e;
+  if (nt == 0) return THERIA_OK;
+  if (!x || !w || !gy || !dx || !dw || !dgy) return THERIA_ERR_INVALID_ARG;
+  if (R == 0) {
+    cudaMemsetAsync(dw, 0, nt * D * sizeof(float), (cudaStream_t)stream);
+    return THERIA_OK;
+  }
+  if (!workspace || workspace_bytes < theria_ln_workspace_bytes(nt, R, D))
+    return THERIA_ERR_WORKSPACE;
+  return ln_dispatch<LnBwd2>(D, x, w, ldw, gy, u, a, c, dx, dw, dgy, (float*)workspace, nt, R,
+                             (int)D, eps, (cudaStream_t)stream);
 }
 
 }  // extern "C"

@@ -1,0 +1,120 @@
+"""Task-batched LayerNorm with per-task affine parameters, twice
+differentiable, on the fused kernels of libtheria_sm100.so
+(``include/theria_ln.h``).
+
+``layer_norm(x, w, b)`` with x ``[nt, ..., D]`` and w, b ``[nt, D]`` (one
+row of fast weights per task) equals
+``F.layer_norm(x, (D,)) * w[:, None, ...] + b[:, None, ...]``.  On CUDA
+tensors the forward is one kernel, the backward one kernel plus a
+deterministic column sum, and the backward's own backward (what the outer
+step of full MAML differentiates through) the same; composed from torch
+operators, that second derivative is several dozen small kernels per call.
+CPU tensors take the composed torch form (the CPU model of the tests); on a
+CUDA tensor the fused kernels are the only path and a missing library
+raises.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+from torch.autograd.function import once_differentiable
+
+from theria_b200 import _lib
+
+EPS = 1e-5
+
+
+def _rows(x, w):
+    nt, D = w.shape
+    return nt, x.numel() // (nt * D), D
+
+
+def _ldw(w):
+    if w.stride(1) != 1:
+        raise ValueError("layer_norm: affine rows must be contiguous")
+    return w.stride(0)
+
+
+def _ws(nt, R, D, like):
+    n = _lib.load().theria_ln_workspace_bytes(nt, R, D)
+    return torch.empty(max(n, 4) // 4, dtype=torch.float32, device=like.device)
+
+
+class _LayerNormBackward(torch.autograd.Function):
+    """(x, w, gy) -> (gx, gw, gb); its backward is the second derivative."""
+
+    @staticmethod
+    def forward(ctx, x, w, gy):
+        gy = gy.contiguous()
+        nt, R, D = _rows(x, w)
+        gx = torch.empty_like(x)
+        gw = torch.empty(nt, D, dtype=x.dtype, device=x.device)
+        gb = torch.empty_like(gw)
+        ws = _ws(nt, R, D, x)
+        _lib.check(_lib.load().theria_ln_bwd(
+            _lib.ptr(x), _lib.ptr(w), _ldw(w), _lib.ptr(gy), _lib.ptr(gx), _lib.ptr(gw),
+            _lib.ptr(gb), _lib.ptr(ws), ws.numel() * 4, nt, R, D, EPS, _lib.stream_of(x)),
+            "theria_ln_bwd")
+        ctx.save_for_backward(x, w, gy)
+        return gx, gw, gb
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, u, a, c):
+        x, w, gy = ctx.saved_tensors
+        nt, R, D = _rows(x, w)
+        u = None if u is None else u.contiguous()
+        a = None if a is None else a.contiguous()
+        c = None if c is None else c.contiguous()
+        dx = torch.empty_like(x)
+        dgy = torch.empty_like(x)
+        dw = torch.empty(nt, D, dtype=x.dtype, device=x.device)
+        ws = _ws(nt, R, D, x)
+        _lib.check(_lib.load().theria_ln_bwd2(
+            _lib.ptr(x), _lib.ptr(w), _ldw(w), _lib.ptr(gy), _lib.ptr(u), _lib.ptr(a),
+            _lib.ptr(c), _lib.ptr(dx), _lib.ptr(dw), _lib.ptr(dgy), _lib.ptr(ws),
+            ws.numel() * 4, nt, R, D, EPS, _lib.stream_of(x)), "theria_ln_bwd2")
+        return dx, dw, dgy
+
+
+class _LayerNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, b):
+        nt, R, D = _rows(x, w)
+        if b.stride() != w.stride():
+            b = b.clone(memory_format=torch.contiguous_format)
+            w = w.contiguous()
+        y = torch.empty_like(x)
+        _lib.check(_lib.load().theria_ln_fwd(
+            _lib.ptr(x), _lib.ptr(w), _lib.ptr(b), _ldw(w), _lib.ptr(y), nt, R, D, EPS,
+            _lib.stream_of(x)), "theria_ln_fwd")
+        ctx.save_for_backward(x, w)
+        return y
+
+    @staticmethod
+    def backward(ctx, gy):
+        x, w = ctx.saved_tensors
+        gx, gw, gb = _LayerNormBackward.apply(x, w, gy)
+        return gx, gw, gb
+
+
+def layer_norm_reference(x, w, b):
+    """The composed torch form (CPU tensors, and the tests' reference)."""
+    h = F.layer_norm(x, (x.shape[-1],), eps=EPS)
+    view = (x.shape[0],) + (1,) * (x.ndim - 2) + (x.shape[-1],)
+    return h * w.view(view) + b.view(view)
+
+
+def layer_norm(x, w, b):
+    """LayerNorm over the last dim of x [nt, ..., D] with per-task w, b [nt, D]."""
+    if not x.is_cuda:
+        return layer_norm_reference(x, w, b)
+    if x.dtype != torch.float32 or w.dtype != torch.float32 or b.dtype != torch.float32:
+        raise ValueError("layer_norm: the fused kernels take float32")
+    if w.shape != (x.shape[0], x.shape[-1]) or b.shape != w.shape:
+        raise ValueError(f"layer_norm: w, b must be [nt, D], got {tuple(w.shape)}")
+    return _LayerNorm.apply(x.contiguous(), w, b)
+
+
+__all__ = ["layer_norm", "layer_norm_reference", "EPS"]

@@ -23,6 +23,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from theria_b200.attention.fused import sdpa_fused
+from theria_b200.maml.layer_norm import layer_norm
 
 
 @dataclass(frozen=True)
@@ -45,9 +46,8 @@ def _linear(h, w, b):
 
 
 def _layer_norm(h, w, b):
-    h = F.layer_norm(h, (h.shape[-1],))
-    view = (h.shape[0],) + (1,) * (h.ndim - 2) + (h.shape[-1],)
-    return h * w.view(view) + b.view(view)
+    # fused kernels on CUDA tensors (twice differentiable), torch ops on CPU
+    return layer_norm(h, w, b)
 
 
 class MAMLClassifier(nn.Module):
