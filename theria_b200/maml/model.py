@@ -24,6 +24,7 @@ import torch.nn.functional as F
 
 from theria_b200.attention.fused import sdpa_fused
 from theria_b200.maml.layer_norm import layer_norm
+from theria_b200.maml.task_bmm import tbmm
 
 
 @dataclass(frozen=True)
@@ -38,10 +39,11 @@ class ModelConfig:
 
 
 def _linear(h, w, b):
-    # h (nt, ..., din), w (nt, dout, din), b (nt, dout)
+    # h (nt, ..., din), w (nt, dout, din), b (nt, dout).  tbmm: the weight
+    # gradients reduce over all rows of a task, which tbmm splits.
     nt = h.shape[0]
     shp = h.shape
-    out = torch.baddbmm(b.unsqueeze(1), h.reshape(nt, -1, shp[-1]), w.transpose(1, 2))
+    out = tbmm(h.reshape(nt, -1, shp[-1]), w.transpose(1, 2)) + b.unsqueeze(1)
     return out.view(*shp[:-1], w.shape[1])
 
 
@@ -93,7 +95,7 @@ class MAMLClassifier(nn.Module):
         # gradient's gradient) is then a batched GEMM, not a sort-based
         # scatter-add; exact in fp32 (one nonzero term per output).
         onehot = F.one_hot(x.reshape(nt, n * L), cfg.vocab).to(params["tok"].dtype)
-        h = torch.bmm(onehot, params["tok"]).view(nt, n, L, D)
+        h = tbmm(onehot, params["tok"]).view(nt, n, L, D)
         h = h + params["pos"][:, :L].unsqueeze(1)
         for i in range(cfg.n_layers):
             p = lambda s: params[f"blocks.{i}.{s}"]  # noqa: E731
