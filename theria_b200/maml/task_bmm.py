@@ -28,11 +28,25 @@ def _split(n, m, k, p):
     return s
 
 
+def _k_major(x):
+    # [n, r, k] stored k-major (x.transpose(1, 2) row-major): the rows of
+    # every k-chunk are then a plain batch of views
+    return x.stride(1) == 1 and x.stride(0) == x.shape[2] * x.stride(2)
+
+
+def _row_major(x):
+    return x.stride(2) == 1 and x.stride(0) == x.shape[1] * x.stride(1)
+
+
+def _transposed(x):
+    return x.stride(1) == 1 and x.stride(2) != 1
+
+
 def _bmm(a, b):
     n, m, k = a.shape
     p = b.shape[2]
     s = _split(n, m, k, p)
-    if s == 1:
+    if s == 1 or not (_k_major(a) and _row_major(b)):
         return torch.bmm(a, b)
     at = a.transpose(1, 2).reshape(n * s, k // s, m).transpose(1, 2)
     bt = b.reshape(n * s, k // s, p)
@@ -47,9 +61,16 @@ class _TaskBmm(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, g):
+        # Each gradient is produced in its input's layout (a transposed view
+        # gets a transposed view back), so no copy follows in autograd.
         a, b = ctx.saved_tensors
-        ga = tbmm(g, b.transpose(1, 2)) if ctx.needs_input_grad[0] else None
-        gb = tbmm(a.transpose(1, 2), g) if ctx.needs_input_grad[1] else None
+        ga = gb = None
+        if ctx.needs_input_grad[0]:
+            ga = (tbmm(b, g.transpose(1, 2)).transpose(1, 2) if _transposed(a)
+                  else tbmm(g, b.transpose(1, 2)))
+        if ctx.needs_input_grad[1]:
+            gb = (tbmm(g.transpose(1, 2), a).transpose(1, 2) if _transposed(b)
+                  else tbmm(a.transpose(1, 2), g))
         return ga, gb
 
 
