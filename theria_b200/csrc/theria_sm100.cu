@@ -789,7 +789,7 @@ struct LnBwd {
     dim3 grid((unsigned)ln_ctas(R), (unsigned)nt);
     ln::bwd_kernel<V><<<grid, ln::WARPS * 32, 0, st>>>(x, w, ldw, gy, gx, ws, R, D, eps);
     if (int e = launch_status()) return e;
-    ln::colsum_kernel<<<(unsigned)nt, 256, 0, st>>>(ws, gw, gb, (int)grid.x, 2, D);
+    ln::colsum_kernel<<<(unsigned)nt, ln::COLSUM_THREADS, 0, st>>>(ws, gw, gb, (int)grid.x, 2, D);
     return launch_status();
   }
 };
@@ -802,7 +802,7 @@ struct LnBwd2 {
     ln::bwd2_kernel<V><<<grid, ln::WARPS * 32, 0, st>>>(x, w, ldw, gy, u, a, c, dx, dgy, ws,
                                                        R, D, eps);
     if (int e = launch_status()) return e;
-    ln::colsum_kernel<<<(unsigned)nt, 256, 0, st>>>(ws, dw, dw, (int)grid.x, 1, D);
+    ln::colsum_kernel<<<(unsigned)nt, ln::COLSUM_THREADS, 0, st>>>(ws, dw, dw, (int)grid.x, 1, D);
     return launch_status();
   }
 };

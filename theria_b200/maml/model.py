@@ -102,7 +102,8 @@ class MAMLClassifier(nn.Module):
             a = _layer_norm(h, p("ln1_w"), p("ln1_b"))
             qkv = _linear(a, p("qkv_w"), p("qkv_b")).view(nt * n, L, 3, H, Dh)
             qkv = qkv.permute(2, 0, 3, 1, 4)  # (3, nt*n, H, L, Dh)
-            o = self.attn_fn(qkv[0], qkv[1], qkv[2])  # (nt*n, H, L, Dh)
+            q, k, v = qkv.unbind(0)  # one stack in the backward, not 3 scatters
+            o = self.attn_fn(q, k, v)  # (nt*n, H, L, Dh)
             o = o.transpose(1, 2).reshape(nt, n, L, D)
             h = h + _linear(o, p("out_w"), p("out_b"))
             f = _layer_norm(h, p("ln2_w"), p("ln2_b"))
