@@ -46,6 +46,10 @@ int theria_ln_bwd2(const float* x, const float* w, int64_t ldw, const float* gy,
                    float* dgy, void* workspace, int64_t workspace_bytes, int64_t nt,
                    int64_t R, int64_t D, float eps, void* stream);
 
+/* out[t][c] = sum_r x[t][r][c] for x [nt, R, C] float32 contiguous (the
+ * bias gradient of the model's task-batched linears); deterministic. */
+int theria_rowsum(const float* x, float* out, int64_t nt, int64_t R, int64_t C, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -75,3 +75,31 @@ def test_layer_norm_refuses_non_float32():
     w = torch.ones(2, 64, device="cuda", dtype=torch.float16)
     with pytest.raises(ValueError):
         layer_norm(x, w, w)
+
+
+def test_task_linear_first_and_second_derivatives():
+    # tbmm (split long reductions) + add_bias (row-sum bias gradient), as the
+    # model's linears use them, against plain torch in float64
+    from theria_b200.maml.task_bmm import add_bias, tbmm
+    g = torch.Generator("cpu").manual_seed(7)
+    h0 = torch.randn(3, 1600, 64, generator=g)
+    flat0 = torch.randn(3, 70 * 64 + 70 + 30, generator=g)
+    r0 = torch.randn(3, 1600, 70, generator=g)
+    v0 = torch.randn(3, 1600, 64, generator=g)
+
+    def run(lin, dev, dt):
+        h = h0.to(dev, dt).requires_grad_(True)
+        flat = flat0.to(dev, dt).requires_grad_(True)
+        w = flat[:, :70 * 64].view(3, 70, 64)
+        b = flat[:, 70 * 64 + 30:]
+        y = lin(h, w, b)
+        gh, gflat = torch.autograd.grad((y.square() * r0.to(dev, dt)).sum(), (h, flat),
+                                        create_graph=True)
+        l2 = (gh * v0.to(dev, dt)).sum() + gflat.square().sum()
+        return (y, gh, gflat) + torch.autograd.grad(l2, (h, flat))
+
+    got = run(lambda h, w, b: add_bias(tbmm(h, w.transpose(1, 2)), b), "cuda", torch.float32)
+    ref = run(lambda h, w, b: torch.bmm(h, w.transpose(1, 2)) + b.unsqueeze(1), "cpu",
+              torch.float64)
+    for a, b in zip(got, ref):
+        assert _rel(a, b) <= 1e-5

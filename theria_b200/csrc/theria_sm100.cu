@@ -839,6 +839,17 @@ int theria_ln_bwd(const float* x, const float* w, int64_t ldw, const float* gy, 
                             eps, (cudaStream_t)stream);
 }
 
+int theria_rowsum(const float* x, float* out, int64_t nt, int64_t R, int64_t C,
+                  void* stream) {
+  if (nt < 0 || R < 0 || C <= 0) return THERIA_ERR_INVALID_ARG;
+  if (nt > 2147483647ll || (C + 31) / 32 > 65535) return THERIA_ERR_UNSUPPORTED;
+  if (nt == 0) return THERIA_OK;
+  if (!x || !out) return THERIA_ERR_INVALID_ARG;
+  dim3 grid((unsigned)nt, (unsigned)((C + 31) / 32));
+  ln::rowsum_kernel<<<grid, ln::ROWSUM_WARPS * 32, 0, (cudaStream_t)stream>>>(x, out, R, (int)C);
+  return launch_status();
+}
+
 int theria_ln_bwd2(const float* x, const float* w, int64_t ldw, const float* gy,
                    const float* u, const float* a, const float* c, float* dx, float* dw,
                    float* dgy, void* workspace, int64_t workspace_bytes, int64_t nt,

@@ -24,7 +24,7 @@ import torch.nn.functional as F
 
 from theria_b200.attention.fused import sdpa_fused
 from theria_b200.maml.layer_norm import layer_norm
-from theria_b200.maml.task_bmm import tbmm
+from theria_b200.maml.task_bmm import add_bias, tbmm
 
 
 @dataclass(frozen=True)
@@ -43,7 +43,7 @@ def _linear(h, w, b):
     # gradients reduce over all rows of a task, which tbmm splits.
     nt = h.shape[0]
     shp = h.shape
-    out = tbmm(h.reshape(nt, -1, shp[-1]), w.transpose(1, 2)) + b.unsqueeze(1)
+    out = add_bias(tbmm(h.reshape(nt, -1, shp[-1]), w.transpose(1, 2)), b)
     return out.view(*shp[:-1], w.shape[1])
 
 

@@ -15,6 +15,8 @@ from __future__ import annotations
 
 import torch
 
+from theria_b200 import _lib
+
 _TARGET_CTAS = 296  # two waves of 64 x 64 output tiles on 148 SMs
 _MIN_CHUNK = 128
 
@@ -79,4 +81,45 @@ def tbmm(a, b):
     return _TaskBmm.apply(a, b)
 
 
-__all__ = ["tbmm"]
+class _RowSum(torch.autograd.Function):
+    """x [n, R, C] -> sum over R, one deterministic kernel on CUDA."""
+
+    @staticmethod
+    def forward(ctx, x):
+        x = x.contiguous()
+        ctx.shape = x.shape
+        if not x.is_cuda:
+            return x.sum(1)
+        out = torch.empty(x.shape[0], x.shape[2], dtype=x.dtype, device=x.device)
+        _lib.check(_lib.load().theria_rowsum(_lib.ptr(x), _lib.ptr(out), x.shape[0],
+                                             x.shape[1], x.shape[2], _lib.stream_of(x)),
+                   "theria_rowsum")
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        return g.unsqueeze(1).expand(ctx.shape)
+
+
+class _AddBias(torch.autograd.Function):
+    """x [n, R, C] + b [n, C] broadcast over R; the bias gradient is a
+    row sum (differentiable: its backward is a broadcast)."""
+
+    @staticmethod
+    def forward(ctx, x, b):
+        return x + b.unsqueeze(1)
+
+    @staticmethod
+    def backward(ctx, g):
+        gb = _RowSum.apply(g) if ctx.needs_input_grad[1] else None
+        return g, gb
+
+
+def add_bias(x, b):
+    """``x + b[:, None, :]`` for x [n, R, C] float32 with a fused bias gradient."""
+    if x.dtype != torch.float32 or not x.is_cuda:
+        return x + b.unsqueeze(1)
+    return _AddBias.apply(x, b)
+
+
+__all__ = ["tbmm", "add_bias"]
