@@ -99,4 +99,4 @@ def test_layer_norm_arguments_checked_on_the_host():
         _lib.THERIA_ERR_INVALID_ARG  # ldw < D
     assert lib.theria_ln_bwd(p, p, 64, p, p, p, p, None, 0, 4, 100, 64, 1e-5, None) == \
         _lib.THERIA_ERR_WORKSPACE
-    assert lib.theria_ln_workspace_bytes(4, 100, 64) == 4 * 2 * 2 * 64 * 4
+    assert lib.theria_ln_workspace_bytes(4, 100, 64) == 4 * 7 * 2 * 64 * 4  # ceil(100 / 16) CTAs

@@ -15,7 +15,7 @@
 // with g = gy * w and K = <P(u), g> (per-row dot products over D).
 //
 // One warp per row (each lane keeps D/32 values in registers).  The sums over
-// rows (gw, gb, d w) are formed per CTA of 64 rows of one task into a
+// rows (gw, gb, d w) are formed per CTA of 16 rows of one task into a
 // workspace and added up by a second, deterministic kernel.
 #pragma once
 
@@ -24,7 +24,7 @@
 namespace theria {
 namespace ln {
 
-constexpr int ROWS_PER_CTA = 64;
+constexpr int ROWS_PER_CTA = 16;  // 2 rows per warp: enough CTAs to hide the row latency
 constexpr int WARPS = 8;
 
 __device__ __forceinline__ float wsum(float x) {
@@ -82,7 +82,7 @@ __device__ __forceinline__ void store_row(float* p, const float (&r)[V], int D) 
     if (lane + 32 * i < D) p[lane + 32 * i] = r[i];
 }
 
-// Grid (ceil(R / 64), nt); rows of one task per CTA.
+// Grid (ceil(R / 16), nt); rows of one task per CTA.
 template <int V>
 __global__ void __launch_bounds__(WARPS * 32)
 fwd_kernel(const float* __restrict__ x, const float* __restrict__ w,
