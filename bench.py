@@ -536,13 +536,47 @@ def theria_arm(args, world, rank, local):
     print(json.dumps(line), flush=True)
 
 
+def profile_maml_step(tasks=4, top=25):
+    """Kernel list of one eager full-MAML meta-step at the 8-GPU share (4
+    tasks), from the torch profiler (CUPTI): per kernel name its launches,
+    device time and share."""
+    import collections
+    from torch.profiler import ProfilerActivity, profile
+    from theria_b200.maml.distributed import MetaStep
+    from theria_b200.maml.model import MAMLClassifier, ModelConfig
+    from theria_b200.maml.tasks import sample_tasks, stack_tasks
+    torch.cuda.set_device(0)
+    torch.manual_seed(0)
+    model = MAMLClassifier(ModelConfig()).cuda()
+    ms = MetaStep(model, meta_batch=32, inner_lr=0.4, inner_steps=5, fo=False, world=1,
+                  capturable=True)
+    tb = stack_tasks(sample_tasks(1000, tasks)).to("cuda")
+    for _ in range(3):
+        ms.step(tb)
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        ms.step(tb)
+        torch.cuda.synchronize()
+    cnt, tim = collections.Counter(), collections.Counter()
+    for ev in prof.events():
+        if ev.device_type == torch.autograd.DeviceType.CUDA:
+            cnt[ev.name] += 1
+            tim[ev.name] += ev.device_time
+    total = sum(tim.values())
+    print(f"kernels {sum(cnt.values())}  device time {total / 1000:.2f} ms  (tasks {tasks})")
+    for name, t in tim.most_common(top):
+        print(f"{cnt[name]:5d}  {t:9.1f} us  {100 * t / total:5.1f} %  {name[:110]}")
+
+
 def profile_case(case):
     """A few launches of one operator at a size ncu can capture in minutes
     (inputs still larger than L2): --profile-case fwdbwd|jvp|hvp, or
     maml_heads: forward + HVP of 3,200 fp32 MAML heads [800, 4, 64, 16]
-    (the whole-head kernels)."""
+    (the whole-head kernels); maml_step: kernel list of one meta-step."""
     from theria_b200.attention import ops
     torch.cuda.set_device(0)
+    if case == "maml_step":
+        return profile_maml_step()
     if case == "maml_heads":
         shape = (800, 4, 64, 16)
     elif case == "fwdbwd":
@@ -576,7 +610,7 @@ def main():
                     help="add the configs[4] long-sequence causal sweep to `extra`")
     ap.add_argument("--cpu-budget", type=float, default=12.0,
                     help="seconds of CPU work for the cpu_baseline sample")
-    ap.add_argument("--profile-case", choices=["fwdbwd", "jvp", "hvp", "maml_heads"],
+    ap.add_argument("--profile-case", choices=["fwdbwd", "jvp", "hvp", "maml_heads", "maml_step"],
                     default=None,
                     help="run a few launches of one operator for ncu, print no bench line")
     args = ap.parse_args()

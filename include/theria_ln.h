@@ -47,8 +47,11 @@ int theria_ln_bwd2(const float* x, const float* w, int64_t ldw, const float* gy,
                    int64_t R, int64_t D, float eps, void* stream);
 
 /* out[t][c] = sum_r x[t][r][c] for x [nt, R, C] float32 contiguous (the
- * bias gradient of the model's task-batched linears); deterministic. */
-int theria_rowsum(const float* x, float* out, int64_t nt, int64_t R, int64_t C, void* stream);
+ * bias gradient of the model's task-batched linears), C <= 1024, through a
+ * workspace of theria_rowsum_workspace_bytes(nt, R, C) bytes; deterministic. */
+int64_t theria_rowsum_workspace_bytes(int64_t nt, int64_t R, int64_t C);
+int theria_rowsum(const float* x, float* out, void* workspace, int64_t workspace_bytes,
+                  int64_t nt, int64_t R, int64_t C, void* stream);
 
 #ifdef __cplusplus
 }

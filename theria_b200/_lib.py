@@ -50,7 +50,8 @@ SIGNATURES = {
     "theria_sdpa_probs": (_i, [_vp] * 4 + [_i64] * 5 + [_i, _f, _i, _vp]),
     "theria_launch_count": (_i64, []),
     "theria_ln_workspace_bytes": (_i64, [_i64] * 3),
-    "theria_rowsum": (_i, [_vp, _vp, _i64, _i64, _i64, _vp]),
+    "theria_rowsum_workspace_bytes": (_i64, [_i64] * 3),
+    "theria_rowsum": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp]),
     "theria_ln_fwd": (_i, [_vp, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _f, _vp]),
     "theria_ln_bwd": (_i, [_vp, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _i64,
                            _i64, _i64, _i64, _f, _vp]),

@@ -250,29 +250,33 @@ colsum_kernel(const float* __restrict__ ws, float* __restrict__ out0,
   }
 }
 
-// out[t][c] = sum_r x[t][r][c]  (x [nt, R, C] contiguous): one CTA per task
-// and 32 columns, lanes over columns, warps over interleaved rows, warps'
-// partials added in a fixed order.  The bias gradient of the model's linears.
-constexpr int ROWSUM_WARPS = 32;
-__global__ void __launch_bounds__(ROWSUM_WARPS * 32)
-rowsum_kernel(const float* __restrict__ x, float* __restrict__ out, int64_t R, int C) {
-  __shared__ float part[ROWSUM_WARPS][33];
+// Partial row sums for out[t][c] = sum_r x[t][r][c] (x [nt, R, C]
+// contiguous; the bias gradient of the model's linears): grid (nt, C/32,
+// ceil(R / ROWSUM_ROWS)), lanes over 32 columns, 8 warps over the CTA's rows,
+// warps' partials added in a fixed order into ws[t][chunk][C]; colsum_kernel
+// then adds the chunks (deterministic overall).
+constexpr int ROWSUM_ROWS = 128;
+__global__ void __launch_bounds__(WARPS * 32)
+rowsum_partial_kernel(const float* __restrict__ x, float* __restrict__ ws, int64_t R, int C) {
+  __shared__ float part[WARPS][33];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t t = blockIdx.x;
   const int c = blockIdx.y * 32 + lane;
+  const int64_t r0 = (int64_t)blockIdx.z * ROWSUM_ROWS;
+  const int64_t r1 = R < r0 + ROWSUM_ROWS ? R : r0 + ROWSUM_ROWS;
   float v = 0.f;
   if (c < C) {
     const float* p = x + t * R * C + c;
 #pragma unroll 4
-    for (int64_t r = warp; r < R; r += ROWSUM_WARPS) v += p[r * C];
+    for (int64_t r = r0 + warp; r < r1; r += WARPS) v += p[r * C];
   }
   part[warp][lane] = v;
   __syncthreads();
-  if (warp == 0) {
-    float s = 0.f;
+  if (warp == 0 && c < C) {
+    float sum = 0.f;
 #pragma unroll
-    for (int w = 0; w < ROWSUM_WARPS; ++w) s += part[w][lane];
-    if (c < C) out[t * C + c] = s;
+    for (int w = 0; w < WARPS; ++w) sum += part[w][lane];
+    ws[(t * gridDim.z + blockIdx.z) * C + c] = sum;
   }
 }
 

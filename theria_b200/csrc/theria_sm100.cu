@@ -839,14 +839,31 @@ int theria_ln_bwd(const float* x, const float* w, int64_t ldw, const float* gy, 
                             eps, (cudaStream_t)stream);
 }
 
-int theria_rowsum(const float* x, float* out, int64_t nt, int64_t R, int64_t C,
-                  void* stream) {
+int64_t theria_rowsum_workspace_bytes(int64_t nt, int64_t R, int64_t C) {
+  return nt * ((R + ln::ROWSUM_ROWS - 1) / ln::ROWSUM_ROWS) * C * (int64_t)sizeof(float);
+}
+
+int theria_rowsum(const float* x, float* out, void* workspace, int64_t workspace_bytes,
+                  int64_t nt, int64_t R, int64_t C, void* stream) {
   if (nt < 0 || R < 0 || C <= 0) return THERIA_ERR_INVALID_ARG;
-  if (nt > 2147483647ll || (C + 31) / 32 > 65535) return THERIA_ERR_UNSUPPORTED;
+  const int64_t chunks = (R + ln::ROWSUM_ROWS - 1) / ln::ROWSUM_ROWS;
+  if (nt > 2147483647ll || (C + 31) / 32 > 65535 || chunks > 65535 || C > 1024)
+    return THERIA_ERR_UNSUPPORTED;
   if (nt == 0) return THERIA_OK;
   if (!x || !out) return THERIA_ERR_INVALID_ARG;
-  dim3 grid((unsigned)nt, (unsigned)((C + 31) / 32));
-  ln::rowsum_kernel<<<grid, ln::ROWSUM_WARPS * 32, 0, (cudaStream_t)stream>>>(x, out, R, (int)C);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (R == 0) {
+    cudaMemsetAsync(out, 0, nt * C * sizeof(float), st);
+    return THERIA_OK;
+  }
+  if (!workspace || workspace_bytes < theria_rowsum_workspace_bytes(nt, R, C))
+    return THERIA_ERR_WORKSPACE;
+  float* ws = (float*)workspace;
+  dim3 grid((unsigned)nt, (unsigned)((C + 31) / 32), (unsigned)chunks);
+  ln::rowsum_partial_kernel<<<grid, ln::WARPS * 32, 0, st>>>(x, ws, R, (int)C);
+  if (int e = launch_status()) return e;
+  ln::colsum_kernel<<<(unsigned)nt, ln::COLSUM_THREADS, 0, st>>>(ws, out, out, (int)chunks, 1,
+                                                                 (int)C);
   return launch_status();
 }
 

@@ -90,10 +90,13 @@ class _RowSum(torch.autograd.Function):
         ctx.shape = x.shape
         if not x.is_cuda:
             return x.sum(1)
-        out = torch.empty(x.shape[0], x.shape[2], dtype=x.dtype, device=x.device)
-        _lib.check(_lib.load().theria_rowsum(_lib.ptr(x), _lib.ptr(out), x.shape[0],
-                                             x.shape[1], x.shape[2], _lib.stream_of(x)),
-                   "theria_rowsum")
+        n, r, c = x.shape
+        out = torch.empty(n, c, dtype=x.dtype, device=x.device)
+        lib = _lib.load()
+        wsb = lib.theria_rowsum_workspace_bytes(n, r, c)
+        ws = torch.empty(max(wsb, 4) // 4, dtype=torch.float32, device=x.device)
+        _lib.check(lib.theria_rowsum(_lib.ptr(x), _lib.ptr(out), _lib.ptr(ws), ws.numel() * 4,
+                                     n, r, c, _lib.stream_of(x)), "theria_rowsum")
         return out
 
     @staticmethod
