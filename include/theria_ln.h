@@ -53,6 +53,12 @@ int64_t theria_rowsum_workspace_bytes(int64_t nt, int64_t R, int64_t C);
 int theria_rowsum(const float* x, float* out, void* workspace, int64_t workspace_bytes,
                   int64_t nt, int64_t R, int64_t C, void* stream);
 
+/* Second derivative of the exact GELU through its backward gx = gy *
+ * gelu'(x): for a cotangent u of gx, dgy = u * gelu'(x) and
+ * dx = u * gy * gelu''(x); x, gy, u, dx, dgy hold n float32 each. */
+int theria_gelu_bwd2(const float* x, const float* gy, const float* u, float* dx, float* dgy,
+                     int64_t n, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -103,3 +103,21 @@ def test_task_linear_first_and_second_derivatives():
               torch.float64)
     for a, b in zip(got, ref):
         assert _rel(a, b) <= 1e-5
+
+
+def test_gelu_second_derivative_matches_torch():
+    from theria_b200.maml.layer_norm import gelu
+    g = torch.Generator("cpu").manual_seed(11)
+    x0 = torch.randn(3, 50, 256, generator=g) * 2
+    r0, v0 = torch.randn(3, 50, 256, generator=g), torch.randn(3, 50, 256, generator=g)
+
+    def run(fn, dev, dt):
+        x = x0.to(dev, dt).requires_grad_(True)
+        r = r0.to(dev, dt).requires_grad_(True)
+        y = fn(x)
+        (gx,) = torch.autograd.grad((y * r).sum(), (x,), create_graph=True)
+        return (y, gx) + torch.autograd.grad((gx * v0.to(dev, dt)).sum(), (x, r))
+
+    for a, b in zip(run(gelu, "cuda", torch.float32),
+                    run(torch.nn.functional.gelu, "cpu", torch.float64)):
+        assert _rel(a, b) <= 1e-5

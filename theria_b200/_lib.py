@@ -51,6 +51,7 @@ SIGNATURES = {
     "theria_launch_count": (_i64, []),
     "theria_ln_workspace_bytes": (_i64, [_i64] * 3),
     "theria_rowsum_workspace_bytes": (_i64, [_i64] * 3),
+    "theria_gelu_bwd2": (_i, [_vp] * 5 + [_i64, _vp]),
     "theria_rowsum": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp]),
     "theria_ln_fwd": (_i, [_vp, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _f, _vp]),
     "theria_ln_bwd": (_i, [_vp, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _i64,

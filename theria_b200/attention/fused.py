@@ -34,11 +34,13 @@ class SDPABackward(torch.autograd.Function):
     """(q, k, v, O, lse, dO) -> (dQ, dK, dV); differentiable once more."""
 
     @staticmethod
-    def forward(ctx, q, k, v, o, lse, dout, causal, scale):
+    def forward(ctx, q, k, v, o, lse, dout, causal, scale, packed=None):
         # q, k, v are the forward's own inputs (possibly strided views): they
         # must stay the tensors autograd knows, or the second-order path
-        # through them is cut.  Packed copies feed the kernels only.
-        qc, kc, vc = q.contiguous(), k.contiguous(), v.contiguous()
+        # through them is cut.  Packed copies feed the kernels only; the
+        # forward's own packed copies come in `packed` (no second packing).
+        qc, kc, vc = packed if packed is not None else (q.contiguous(), k.contiguous(),
+                                                        v.contiguous())
         dout = _c(dout, q.dtype)
         dq, dk, dv = ops.backward(qc, kc, vc, dout, lse, o=o, causal=causal, scale=scale)
         ctx.save_for_backward(qc, kc, vc, lse, dout)
@@ -56,7 +58,7 @@ class SDPABackward(torch.autograd.Function):
         hq, hk, hv, ot = ops.hvp(q, k, v, dout, lse, tq, tk, tv, causal=ctx.causal,
                                  scale=ctx.scale,
                                  need=(need[0], need[1], need[2], need[5]))
-        return hq, hk, hv, None, None, ot, None, None
+        return hq, hk, hv, None, None, ot, None, None, None
 
 
 class SDPAFunction(torch.autograd.Function):
@@ -68,18 +70,17 @@ class SDPAFunction(torch.autograd.Function):
         # Strided views (e.g. heads split out of a fused projection) are
         # packed for the kernels, but the saved q, k, v are the inputs
         # themselves so that the backward Function stays connected to them.
-        o, lse = ops.forward(q.contiguous(), k.contiguous(), v.contiguous(), causal=causal,
-                             scale=scale)
-        ctx.save_for_backward(q, k, v, o, lse)
-        ctx.save_for_forward(q, k, v, lse)
+        qc, kc, vc = q.contiguous(), k.contiguous(), v.contiguous()
+        o, lse = ops.forward(qc, kc, vc, causal=causal, scale=scale)
+        ctx.save_for_backward(q, k, v, o, lse, qc, kc, vc)
+        ctx.save_for_forward(q, k, v, lse, qc, kc, vc)
         ctx.causal, ctx.scale = causal, scale
         return o
 
     @staticmethod
     def jvp(ctx, tq, tk, tv, _causal=None, _scale=None):
         """Forward-mode rule (torch.autograd.forward_ad): the JVP kernel."""
-        q, k, v, lse = ctx.saved_tensors
-        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+        _, _, _, lse, q, k, v = ctx.saved_tensors
         tq = torch.zeros_like(q) if tq is None else _c(tq, q.dtype)
         tk = torch.zeros_like(k) if tk is None else _c(tk, k.dtype)
         tv = torch.zeros_like(v) if tv is None else _c(tv, v.dtype)
@@ -87,8 +88,9 @@ class SDPAFunction(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, grad_out):
-        q, k, v, o, lse = ctx.saved_tensors
-        dq, dk, dv = SDPABackward.apply(q, k, v, o, lse, grad_out, ctx.causal, ctx.scale)
+        q, k, v, o, lse, qc, kc, vc = ctx.saved_tensors
+        dq, dk, dv = SDPABackward.apply(q, k, v, o, lse, grad_out, ctx.causal, ctx.scale,
+                                        (qc, kc, vc))
         return dq, dk, dv, None, None
 
     @staticmethod

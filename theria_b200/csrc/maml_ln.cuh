@@ -280,5 +280,24 @@ rowsum_partial_kernel(const float* __restrict__ x, float* __restrict__ ws, int64
   }
 }
 
+// Second derivative of the exact (erf) GELU through its backward
+// gx = gy * gelu'(x): for a cotangent u of gx,
+//   d gy = u * gelu'(x),   d x = u * gy * gelu''(x),
+// gelu'(x) = Phi(x) + x phi(x),  gelu''(x) = phi(x) (2 - x^2), with the
+// standard normal cdf Phi and density phi.  Elementwise, grid-stride.
+__global__ void gelu_bwd2_kernel(const float* __restrict__ x, const float* __restrict__ gy,
+                                 const float* __restrict__ u, float* __restrict__ dx,
+                                 float* __restrict__ dgy, int64_t n) {
+  const float kInvSqrt2 = 0.70710678118654752f, kInvSqrt2Pi = 0.39894228040143268f;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float xv = x[i], uv = u[i];
+    const float pdf = kInvSqrt2Pi * expf(-0.5f * xv * xv);
+    const float cdf = 0.5f * (1.f + erff(xv * kInvSqrt2));
+    dgy[i] = uv * fmaf(xv, pdf, cdf);
+    dx[i] = uv * gy[i] * pdf * (2.f - xv * xv);
+  }
+}
+
 }  // namespace ln
 }  // namespace theria

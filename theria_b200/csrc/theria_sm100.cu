@@ -839,6 +839,16 @@ int theria_ln_bwd(const float* x, const float* w, int64_t ldw, const float* gy, 
                             eps, (cudaStream_t)stream);
 }
 
+int theria_gelu_bwd2(const float* x, const float* gy, const float* u, float* dx, float* dgy,
+                     int64_t n, void* stream) {
+  if (n < 0) return THERIA_ERR_INVALID_ARG;
+  if (n == 0) return THERIA_OK;
+  if (!x || !gy || !u || !dx || !dgy) return THERIA_ERR_INVALID_ARG;
+  const int64_t blocks = std::min<int64_t>((n + 255) / 256, 148 * 16);
+  ln::gelu_bwd2_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(x, gy, u, dx, dgy, n);
+  return launch_status();
+}
+
 int64_t theria_rowsum_workspace_bytes(int64_t nt, int64_t R, int64_t C) {
   return nt * ((R + ln::ROWSUM_ROWS - 1) / ln::ROWSUM_ROWS) * C * (int64_t)sizeof(float);
 }

@@ -99,6 +99,46 @@ class _LayerNorm(torch.autograd.Function):
         return gx, gw, gb
 
 
+class _GeluBackward(torch.autograd.Function):
+    """(x, gy) -> gy * gelu'(x) (torch's kernel); its backward is one kernel."""
+
+    @staticmethod
+    def forward(ctx, x, gy):
+        gy = gy.contiguous()
+        ctx.save_for_backward(x, gy)
+        return torch.ops.aten.gelu_backward(gy, x)
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, u):
+        x, gy = ctx.saved_tensors
+        u = u.contiguous()
+        dx, dgy = torch.empty_like(x), torch.empty_like(x)
+        _lib.check(_lib.load().theria_gelu_bwd2(
+            _lib.ptr(x), _lib.ptr(gy), _lib.ptr(u), _lib.ptr(dx), _lib.ptr(dgy), x.numel(),
+            _lib.stream_of(x)), "theria_gelu_bwd2")
+        return dx, dgy
+
+
+class _Gelu(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x):
+        ctx.save_for_backward(x)
+        return F.gelu(x)
+
+    @staticmethod
+    def backward(ctx, gy):
+        (x,) = ctx.saved_tensors
+        return _GeluBackward.apply(x, gy)
+
+
+def gelu(x):
+    """Exact GELU; on CUDA float32 its second derivative is one kernel."""
+    if not x.is_cuda or x.dtype != torch.float32:
+        return F.gelu(x)
+    return _Gelu.apply(x.contiguous())
+
+
 def layer_norm_reference(x, w, b):
     """The composed torch form (CPU tensors, and the tests' reference)."""
     h = F.layer_norm(x, (x.shape[-1],), eps=EPS)
@@ -117,4 +157,4 @@ def layer_norm(x, w, b):
     return _LayerNorm.apply(x.contiguous(), w, b)
 
 
-__all__ = ["layer_norm", "layer_norm_reference", "EPS"]
+__all__ = ["layer_norm", "layer_norm_reference", "gelu", "EPS"]

@@ -23,7 +23,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from theria_b200.attention.fused import sdpa_fused
-from theria_b200.maml.layer_norm import layer_norm
+from theria_b200.maml.layer_norm import gelu, layer_norm
 from theria_b200.maml.task_bmm import add_bias, tbmm
 
 
@@ -107,7 +107,7 @@ class MAMLClassifier(nn.Module):
             o = o.transpose(1, 2).reshape(nt, n, L, D)
             h = h + _linear(o, p("out_w"), p("out_b"))
             f = _layer_norm(h, p("ln2_w"), p("ln2_b"))
-            f = F.gelu(_linear(f, p("ff1_w"), p("ff1_b")))
+            f = gelu(_linear(f, p("ff1_w"), p("ff1_b")))
             h = h + _linear(f, p("ff2_w"), p("ff2_b"))
         h = _layer_norm(h, params["lnf_w"], params["lnf_b"]).mean(dim=2)  # (nt, n, D)
         return _linear(h, params["head_w"], params["head_b"])  # (nt, n, C)
