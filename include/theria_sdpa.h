@@ -176,6 +176,27 @@ int theria_sdpa_probs(const void* q, const void* k, const float* lse, float* out
                       int64_t B, int64_t H, int64_t T, int64_t M, int64_t D,
                       int dtype, float scale, int causal, void* stream);
 
+/* Packed self-attention (T == M) for short sequences (T <= 64, D <= 64,
+ * the whole-head kernels; otherwise THERIA_ERR_UNSUPPORTED): q, k, v are
+ * read in place from a fused projection qkv [B, T, 3, H, D] (q at offset 0,
+ * k at H*D, v at 2*H*D of each token row), O-shaped tensors (o, dout / w,
+ * o_tan) are [B, T, H, D], and gradients (dqkv, hqkv) come back packed like
+ * qkv.  Same arithmetic as theria_sdpa_fwd / _bwd / _hvp; the layout saves
+ * the copies between a [B, T, 3, H, D] projection and [B, H, T, D] heads.
+ * fwd writes o in the input dtype.  hvp: hqkv or o_tan may be NULL.
+ * Replaces no reference entry point: the reference's attention callers
+ * (examples/minimal_decoder_transformer.py:82-263) split heads with
+ * reshape/transpose before calling the attention op. */
+int theria_sdpa_qkv_fwd(const void* qkv, void* o, float* lse, int64_t B, int64_t H,
+                        int64_t T, int64_t D, int dtype, float scale, int causal,
+                        void* stream);
+int theria_sdpa_qkv_bwd(const void* qkv, const void* dout, const float* lse, void* dqkv,
+                        int64_t B, int64_t H, int64_t T, int64_t D, int dtype, float scale,
+                        int causal, void* stream);
+int theria_sdpa_qkv_hvp(const void* qkv, const void* w, const float* lse, const void* tqkv,
+                        void* hqkv, void* o_tan, int64_t B, int64_t H, int64_t T, int64_t D,
+                        int dtype, float scale, int causal, void* stream);
+
 /* Number of kernels this library has launched in this process (all devices,
  * all threads); for accounting in benchmarks and tests. */
 int64_t theria_launch_count(void);

@@ -48,6 +48,9 @@ SIGNATURES = {
     "theria_sdpa_bwd_noalloc": (_i, [_vp] * 10 + [_i64] * 5 + [_i, _f, _i, _vp]),
     "theria_sdpa_scores": (_i, [_vp, _vp, _vp, _i] + [_i64] * 5 + [_i, _f, _vp]),
     "theria_sdpa_probs": (_i, [_vp] * 4 + [_i64] * 5 + [_i, _f, _i, _vp]),
+    "theria_sdpa_qkv_fwd": (_i, [_vp] * 3 + [_i64] * 4 + [_i, _f, _i, _vp]),
+    "theria_sdpa_qkv_bwd": (_i, [_vp] * 4 + [_i64] * 4 + [_i, _f, _i, _vp]),
+    "theria_sdpa_qkv_hvp": (_i, [_vp] * 6 + [_i64] * 4 + [_i, _f, _i, _vp]),
     "theria_launch_count": (_i64, []),
     "theria_ln_workspace_bytes": (_i64, [_i64] * 3),
     "theria_rowsum_workspace_bytes": (_i64, [_i64] * 3),

@@ -22,6 +22,15 @@ constexpr int MAXN = 64;   // max T and M
 constexpr int MAXD = 64;   // max head dim
 constexpr int NTHREADS = 256;
 
+// Element strides (batch, head, row) of the three tensor families; the last
+// dim is contiguous.  q-like: q, tq, dq, hq; k-like: k, v, tk, tv, dk, dv,
+// hk, hv; o-like: o, dO / W, o_tan.  Contiguous [B, H, rows, D] tensors have
+// (H*rows*D, rows*D, D); a packed self-attention projection [B, T, 3, H, D]
+// has (3*H*D*T, D, 3*H*D) for q, k and v alike.
+struct Layout {
+  int64_t qb, qh, qt, kb, kh, kt, ob, oh, ot;
+};
+
 // Arithmetic in the accumulator type A: float for fp32/fp16/bf16 inputs,
 // double for fp64 inputs (the fp64 variant serves gradcheck-style checks).
 __device__ __forceinline__ float fmaA(float a, float b, float c) { return fmaf(a, b, c); }
@@ -48,10 +57,11 @@ inline size_t smem_bytes(int T, int M, int D, int n_q_like, int n_k_like, int n_
 }
 
 template <typename A, typename T>
-__device__ __forceinline__ void load_mat(A* dst, const T* __restrict__ src, int rows, int D) {
+__device__ __forceinline__ void load_mat(A* dst, const T* __restrict__ src, int rows, int D,
+                                         int64_t ld) {
   for (int e = threadIdx.x; e < rows * D; e += blockDim.x) {
     const int r = e / D, d = e - r * D;
-    dst[r * (D + 1) + d] = load_as<A>(src[e]);
+    dst[r * (D + 1) + d] = load_as<A>(src[r * ld + d]);
   }
 }
 
@@ -164,43 +174,43 @@ __device__ __forceinline__ void abt2(A* C, int ldc, const A* A1, const A* B1,
 // out[i][d] = alpha * sum_j (S1[i][j] X1[j][d] [+ S2[i][j] X2[j][d]])
 //   (S: [rS][cS] at stride lds; X: [cS][D] at stride D+1; out: [rS][D] dense)
 template <bool TWO, typename OT, typename A>
-__device__ __forceinline__ void sx_impl(OT* __restrict__ out, const A* S1, const A* X1,
-                                        const A* S2, const A* X2, int lds, int rS,
-                                        int cS, int D, A alpha) {
+__device__ __forceinline__ void sx_impl(OT* __restrict__ out, int64_t ldo, const A* S1,
+                                        const A* X1, const A* S2, const A* X2, int lds,
+                                        int rS, int cS, int D, A alpha) {
   prod<TWO, A>(rS, D, cS, S1, X1, S2, X2, lds, 1, 1, D + 1, alpha,
-               [&](int i, int d, A x) { out[i * D + d] = store_as<OT>(x); });
+               [&](int i, int d, A x) { out[i * ldo + d] = store_as<OT>(x); });
 }
 
 // out[j][d] = alpha * sum_i (S1[i][j] X1[i][d] [+ S2[i][j] X2[i][d]])  (S transposed)
 template <bool TWO, typename OT, typename A>
-__device__ __forceinline__ void stx_impl(OT* __restrict__ out, const A* S1, const A* X1,
-                                         const A* S2, const A* X2, int lds, int rS,
-                                         int cS, int D, A alpha) {
+__device__ __forceinline__ void stx_impl(OT* __restrict__ out, int64_t ldo, const A* S1,
+                                         const A* X1, const A* S2, const A* X2, int lds,
+                                         int rS, int cS, int D, A alpha) {
   prod<TWO, A>(cS, D, rS, S1, X1, S2, X2, 1, lds, 1, D + 1, alpha,
-               [&](int j, int d, A x) { out[j * D + d] = store_as<OT>(x); });
+               [&](int j, int d, A x) { out[j * ldo + d] = store_as<OT>(x); });
 }
 
 template <typename OT, typename A>
-__device__ __forceinline__ void sx(OT* __restrict__ out, const A* S, int lds, const A* X,
-                                   int rS, int cS, int D, A alpha) {
-  sx_impl<false, OT, A>(out, S, X, nullptr, nullptr, lds, rS, cS, D, alpha);
+__device__ __forceinline__ void sx(OT* __restrict__ out, int64_t ldo, const A* S, int lds,
+                                   const A* X, int rS, int cS, int D, A alpha) {
+  sx_impl<false, OT, A>(out, ldo, S, X, nullptr, nullptr, lds, rS, cS, D, alpha);
 }
 template <typename OT, typename A>
-__device__ __forceinline__ void sx2(OT* __restrict__ out, const A* S1, const A* X1,
-                                    const A* S2, const A* X2, int lds, int rS, int cS,
-                                    int D, A alpha) {
-  sx_impl<true, OT, A>(out, S1, X1, S2, X2, lds, rS, cS, D, alpha);
+__device__ __forceinline__ void sx2(OT* __restrict__ out, int64_t ldo, const A* S1,
+                                    const A* X1, const A* S2, const A* X2, int lds, int rS,
+                                    int cS, int D, A alpha) {
+  sx_impl<true, OT, A>(out, ldo, S1, X1, S2, X2, lds, rS, cS, D, alpha);
 }
 template <typename OT, typename A>
-__device__ __forceinline__ void stx(OT* __restrict__ out, const A* S, int lds,
+__device__ __forceinline__ void stx(OT* __restrict__ out, int64_t ldo, const A* S, int lds,
                                     const A* X, int rS, int cS, int D, A alpha) {
-  stx_impl<false, OT, A>(out, S, X, nullptr, nullptr, lds, rS, cS, D, alpha);
+  stx_impl<false, OT, A>(out, ldo, S, X, nullptr, nullptr, lds, rS, cS, D, alpha);
 }
 template <typename OT, typename A>
-__device__ __forceinline__ void stx2(OT* __restrict__ out, const A* S1, const A* X1,
-                                     const A* S2, const A* X2, int lds, int rS, int cS,
-                                     int D, A alpha) {
-  stx_impl<true, OT, A>(out, S1, X1, S2, X2, lds, rS, cS, D, alpha);
+__device__ __forceinline__ void stx2(OT* __restrict__ out, int64_t ldo, const A* S1,
+                                     const A* X1, const A* S2, const A* X2, int lds, int rS,
+                                     int cS, int D, A alpha) {
+  stx_impl<true, OT, A>(out, ldo, S1, X1, S2, X2, lds, rS, cS, D, alpha);
 }
 
 __device__ __forceinline__ bool masked(int i, int j, int causal) { return causal && j > i; }
@@ -256,20 +266,22 @@ __device__ __forceinline__ void probs_from_lse(A* S, int lds, const A* lse_s, in
 template <typename T, typename OT, typename A = float, int NC = 0, int DC = 0>
 __global__ void __launch_bounds__(NTHREADS)
 fwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
-           OT* __restrict__ o, float* __restrict__ lse, Shape s) {
+           OT* __restrict__ o, float* __restrict__ lse, Shape s, Layout ly) {
   extern __shared__ __align__(16) unsigned char sm_raw[];
   A* sm = reinterpret_cast<A*>(sm_raw);
   // NC, DC > 0: sequence lengths and head dim fixed at compile time
   const int Tq = NC ? NC : (int)s.T, M = NC ? NC : (int)s.M, D = DC ? DC : (int)s.D;
   const int lm = M + 1;
-  const int64_t bh = blockIdx.x;
+  const int64_t bh = blockIdx.x, hb = bh / s.H, hh = bh - hb * s.H;
+  const int64_t qo = hb * ly.qb + hh * ly.qh, ko = hb * ly.kb + hh * ly.kh,
+                oo = hb * ly.ob + hh * ly.oh;
   A* Q = sm;
   A* K = Q + Tq * (D + 1);
   A* V = K + M * (D + 1);
   A* S = V + M * (D + 1);
-  load_mat(Q, q + bh * Tq * D, Tq, D);
-  load_mat(K, k + bh * M * D, M, D);
-  load_mat(V, v + bh * M * D, M, D);
+  load_mat(Q, q + qo, Tq, D, ly.qt);
+  load_mat(K, k + ko, M, D, ly.kt);
+  load_mat(V, v + ko, M, D, ly.kt);
   __syncthreads();
   abt(S, lm, Q, K, Tq, M, D, A(s.scale));
   __syncthreads();
@@ -290,7 +302,7 @@ fwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
     if (lse && (threadIdx.x & 31) == 0) lse[bh * Tq + i] = m + logA(l);
   }
   __syncthreads();
-  sx(o + bh * Tq * D, S, lm, V, Tq, M, D, A(1));
+  sx(o + oo, ly.ot, S, lm, V, Tq, M, D, A(1));
 }
 
 // ---------------------------------------------------------------- backward
@@ -298,13 +310,15 @@ template <typename T, typename A = float, int NC = 0, int DC = 0>
 __global__ void __launch_bounds__(NTHREADS)
 bwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
            const T* __restrict__ dout, const float* __restrict__ lse, T* __restrict__ dq,
-           T* __restrict__ dk, T* __restrict__ dv, Shape s) {
+           T* __restrict__ dk, T* __restrict__ dv, Shape s, Layout ly) {
   extern __shared__ __align__(16) unsigned char sm_raw[];
   A* sm = reinterpret_cast<A*>(sm_raw);
   // NC, DC > 0: sequence lengths and head dim fixed at compile time
   const int Tq = NC ? NC : (int)s.T, M = NC ? NC : (int)s.M, D = DC ? DC : (int)s.D;
   const int lm = M + 1;
-  const int64_t bh = blockIdx.x;
+  const int64_t bh = blockIdx.x, hb = bh / s.H, hh = bh - hb * s.H;
+  const int64_t qo = hb * ly.qb + hh * ly.qh, ko = hb * ly.kb + hh * ly.kh,
+                oo = hb * ly.ob + hh * ly.oh;
   A* Q = sm;
   A* G = Q + Tq * (D + 1);  // dO
   A* K = G + Tq * (D + 1);
@@ -312,10 +326,10 @@ bwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
   A* P = V + M * (D + 1);
   A* DS = P + Tq * lm;
   A* L = DS + Tq * lm;
-  load_mat(Q, q + bh * Tq * D, Tq, D);
-  load_mat(G, dout + bh * Tq * D, Tq, D);
-  load_mat(K, k + bh * M * D, M, D);
-  load_mat(V, v + bh * M * D, M, D);
+  load_mat(Q, q + qo, Tq, D, ly.qt);
+  load_mat(G, dout + oo, Tq, D, ly.ot);
+  load_mat(K, k + ko, M, D, ly.kt);
+  load_mat(V, v + ko, M, D, ly.kt);
   for (int i = threadIdx.x; i < Tq; i += blockDim.x) L[i] = lse[bh * Tq + i];
   __syncthreads();
   abt(P, lm, Q, K, Tq, M, D, A(s.scale));
@@ -334,9 +348,9 @@ bwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
     THERIA_COLS(j) ds[j] = p[j] * (ds[j] - z);
   }
   __syncthreads();
-  if (dq) sx(dq + bh * Tq * D, DS, lm, K, Tq, M, D, A(s.scale));
-  if (dk) stx(dk + bh * M * D, DS, lm, Q, Tq, M, D, A(s.scale));
-  if (dv) stx(dv + bh * M * D, P, lm, G, Tq, M, D, A(1));
+  if (dq) sx(dq + qo, ly.qt, DS, lm, K, Tq, M, D, A(s.scale));
+  if (dk) stx(dk + ko, ly.kt, DS, lm, Q, Tq, M, D, A(s.scale));
+  if (dv) stx(dv + ko, ly.kt, P, lm, G, Tq, M, D, A(1));
 }
 
 // ---------------------------------------------------------------- JVP
@@ -344,13 +358,15 @@ template <typename T, typename A = float, int NC = 0, int DC = 0>
 __global__ void __launch_bounds__(NTHREADS)
 jvp_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
            const T* __restrict__ tq, const T* __restrict__ tk, const T* __restrict__ tv,
-           const float* __restrict__ lse, T* __restrict__ o_tan, Shape s) {
+           const float* __restrict__ lse, T* __restrict__ o_tan, Shape s, Layout ly) {
   extern __shared__ __align__(16) unsigned char sm_raw[];
   A* sm = reinterpret_cast<A*>(sm_raw);
   // NC, DC > 0: sequence lengths and head dim fixed at compile time
   const int Tq = NC ? NC : (int)s.T, M = NC ? NC : (int)s.M, D = DC ? DC : (int)s.D;
   const int lm = M + 1;
-  const int64_t bh = blockIdx.x;
+  const int64_t bh = blockIdx.x, hb = bh / s.H, hh = bh - hb * s.H;
+  const int64_t qo = hb * ly.qb + hh * ly.qh, ko = hb * ly.kb + hh * ly.kh,
+                oo = hb * ly.ob + hh * ly.oh;
   A* Q = sm;
   A* TQ = Q + Tq * (D + 1);
   A* K = TQ + Tq * (D + 1);
@@ -360,12 +376,12 @@ jvp_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
   A* P = TV + M * (D + 1);
   A* SD = P + Tq * lm;
   A* L = SD + Tq * lm;
-  load_mat(Q, q + bh * Tq * D, Tq, D);
-  load_mat(TQ, tq + bh * Tq * D, Tq, D);
-  load_mat(K, k + bh * M * D, M, D);
-  load_mat(TK, tk + bh * M * D, M, D);
-  load_mat(V, v + bh * M * D, M, D);
-  load_mat(TV, tv + bh * M * D, M, D);
+  load_mat(Q, q + qo, Tq, D, ly.qt);
+  load_mat(TQ, tq + qo, Tq, D, ly.qt);
+  load_mat(K, k + ko, M, D, ly.kt);
+  load_mat(TK, tk + ko, M, D, ly.kt);
+  load_mat(V, v + ko, M, D, ly.kt);
+  load_mat(TV, tv + ko, M, D, ly.kt);
   for (int i = threadIdx.x; i < Tq; i += blockDim.x) L[i] = lse[bh * Tq + i];
   __syncthreads();
   abt(P, lm, Q, K, Tq, M, D, A(s.scale));
@@ -384,7 +400,7 @@ jvp_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
     THERIA_COLS(j) sd[j] = p[j] * (sd[j] - c);
   }
   __syncthreads();
-  sx2(o_tan + bh * Tq * D, SD, V, P, TV, lm, Tq, M, D, A(1));
+  sx2(o_tan + oo, ly.ot, SD, V, P, TV, lm, Tq, M, D, A(1));
 }
 
 // ---------------------------------------------------------------- HVP
@@ -394,13 +410,15 @@ __global__ void __launch_bounds__(NTHREADS)
 hvp_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
            const T* __restrict__ w, const float* __restrict__ lse, const T* __restrict__ tq,
            const T* __restrict__ tk, const T* __restrict__ tv, T* __restrict__ hq,
-           T* __restrict__ hk, T* __restrict__ hv, T* __restrict__ o_tan, Shape s) {
+           T* __restrict__ hk, T* __restrict__ hv, T* __restrict__ o_tan, Shape s, Layout ly) {
   extern __shared__ __align__(16) unsigned char sm_raw[];
   A* sm = reinterpret_cast<A*>(sm_raw);
   // NC, DC > 0: sequence lengths and head dim fixed at compile time
   const int Tq = NC ? NC : (int)s.T, M = NC ? NC : (int)s.M, D = DC ? DC : (int)s.D;
   const int lm = M + 1;
-  const int64_t bh = blockIdx.x;
+  const int64_t bh = blockIdx.x, hb = bh / s.H, hh = bh - hb * s.H;
+  const int64_t qo = hb * ly.qb + hh * ly.qh, ko = hb * ly.kb + hh * ly.kh,
+                oo = hb * ly.ob + hh * ly.oh;
   const int qsz = Tq * (D + 1), ksz = M * (D + 1), ssz = Tq * lm;
   A* Q = sm;
   A* TQ = Q + qsz;
@@ -414,14 +432,13 @@ hvp_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
   A* DS = PD + ssz;  // dP   -> dS
   A* DSD = DS + ssz; // dPd  -> dSd
   A* L = DSD + ssz;
-  const int64_t qo = bh * Tq * D, ko = bh * M * D;
-  load_mat(Q, q + qo, Tq, D);
-  load_mat(TQ, tq + qo, Tq, D);
-  load_mat(W, w + qo, Tq, D);
-  load_mat(K, k + ko, M, D);
-  load_mat(TK, tk + ko, M, D);
-  load_mat(V, v + ko, M, D);
-  load_mat(TV, tv + ko, M, D);
+  load_mat(Q, q + qo, Tq, D, ly.qt);
+  load_mat(TQ, tq + qo, Tq, D, ly.qt);
+  load_mat(W, w + oo, Tq, D, ly.ot);
+  load_mat(K, k + ko, M, D, ly.kt);
+  load_mat(TK, tk + ko, M, D, ly.kt);
+  load_mat(V, v + ko, M, D, ly.kt);
+  load_mat(TV, tv + ko, M, D, ly.kt);
   for (int i = threadIdx.x; i < Tq; i += blockDim.x) L[i] = lse[bh * Tq + i];
   __syncthreads();
   abt(P, lm, Q, K, Tq, M, D, A(s.scale));
@@ -458,10 +475,10 @@ hvp_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
     }
   }
   __syncthreads();
-  if (hq) sx2(hq + qo, DSD, K, DS, TK, lm, Tq, M, D, A(s.scale));
-  if (hk) stx2(hk + ko, DSD, Q, DS, TQ, lm, Tq, M, D, A(s.scale));
-  if (hv) stx(hv + ko, PD, lm, W, Tq, M, D, A(1));
-  if (o_tan) sx2(o_tan + qo, PD, V, P, TV, lm, Tq, M, D, A(1));
+  if (hq) sx2(hq + qo, ly.qt, DSD, K, DS, TK, lm, Tq, M, D, A(s.scale));
+  if (hk) stx2(hk + ko, ly.kt, DSD, Q, DS, TQ, lm, Tq, M, D, A(s.scale));
+  if (hv) stx(hv + ko, ly.kt, PD, lm, W, Tq, M, D, A(1));
+  if (o_tan) sx2(o_tan + oo, ly.ot, PD, V, P, TV, lm, Tq, M, D, A(1));
 }
 
 #undef THERIA_ROWS

@@ -187,6 +187,19 @@ bool small_spec(const Shape& s) {
          s.M == 64 && s.D == 16;
 }
 
+// Strides of contiguous [B, H, rows, D] tensors.
+small::Layout contiguous_layout(const Shape& s) {
+  const int64_t q = s.T * s.D, k = s.M * s.D;
+  return small::Layout{s.H * q, q, s.D, s.H * k, k, s.D, s.H * q, q, s.D};
+}
+// Packed self-attention: q, k, v (and their gradients) at offsets 0, H*D,
+// 2*H*D of [B, T, 3, H, D]; O-shaped tensors [B, T, H, D].
+small::Layout packed_layout(const Shape& s) {
+  const int64_t hd = s.H * s.D;
+  return small::Layout{3 * hd * s.T, s.D, 3 * hd, 3 * hd * s.T, s.D, 3 * hd,
+                       hd * s.T, s.D, hd};
+}
+
 template <typename K>
 void small_setup(K kern, size_t bytes) {
   if (bytes > 48 * 1024)
@@ -195,7 +208,8 @@ void small_setup(K kern, size_t bytes) {
 
 template <typename T, typename A = float>
 int small_fwd(const void* q, const void* k, const void* v, void* o, int o_dtype, float* lse,
-              const Shape& s, cudaStream_t st) {
+              const Shape& s, cudaStream_t st, const small::Layout* lyp = nullptr) {
+  const small::Layout ly = lyp ? *lyp : contiguous_layout(s);
   const size_t sm = small::smem_bytes((int)s.T, (int)s.M, (int)s.D, 1, 2, 1, sizeof(A));
   const unsigned grid = (unsigned)(s.B * s.H);
   if (o_dtype == THERIA_F32) {
@@ -204,34 +218,39 @@ int small_fwd(const void* q, const void* k, const void* v, void* o, int o_dtype,
       if (small_spec<T, A>(s)) kern = small::fwd_kernel<T, float, A, 64, 16>;
     small_setup(kern, sm);
     kern<<<grid, small::NTHREADS, sm, st>>>((const T*)q, (const T*)k, (const T*)v, (float*)o,
-                                            lse, s);
+                                            lse, s, ly);
   } else {
     auto kern = small::fwd_kernel<T, T, A>;
     if constexpr (std::is_same<T, float>::value && std::is_same<A, float>::value)
       if (small_spec<T, A>(s)) kern = small::fwd_kernel<T, T, A, 64, 16>;
     small_setup(kern, sm);
     kern<<<grid, small::NTHREADS, sm, st>>>((const T*)q, (const T*)k, (const T*)v, (T*)o, lse,
-                                            s);
+                                            s, ly);
   }
   return launch_status();
 }
 
 template <typename T, typename A = float>
 int small_bwd(const void* q, const void* k, const void* v, const void* dout, const float* lse,
-              void* dq, void* dk, void* dv, const Shape& s, cudaStream_t st) {
+              void* dq, void* dk, void* dv, const Shape& s, cudaStream_t st,
+              const small::Layout* lyp = nullptr) {
+  const small::Layout ly = lyp ? *lyp : contiguous_layout(s);
   const size_t sm = small::smem_bytes((int)s.T, (int)s.M, (int)s.D, 2, 2, 2, sizeof(A));
   auto kern = small::bwd_kernel<T, A>;
   if constexpr (std::is_same<T, float>::value && std::is_same<A, float>::value)
     if (small_spec<T, A>(s)) kern = small::bwd_kernel<T, A, 64, 16>;
   small_setup(kern, sm);
   kern<<<(unsigned)(s.B * s.H), small::NTHREADS, sm, st>>>(
-      (const T*)q, (const T*)k, (const T*)v, (const T*)dout, lse, (T*)dq, (T*)dk, (T*)dv, s);
+      (const T*)q, (const T*)k, (const T*)v, (const T*)dout, lse, (T*)dq, (T*)dk, (T*)dv, s,
+      ly);
   return launch_status();
 }
 
 template <typename T, typename A = float>
 int small_jvp(const void* q, const void* k, const void* v, const void* tq, const void* tk,
-              const void* tv, const float* lse, void* o_tan, const Shape& s, cudaStream_t st) {
+              const void* tv, const float* lse, void* o_tan, const Shape& s, cudaStream_t st,
+              const small::Layout* lyp = nullptr) {
+  const small::Layout ly = lyp ? *lyp : contiguous_layout(s);
   const size_t sm = small::smem_bytes((int)s.T, (int)s.M, (int)s.D, 2, 4, 2, sizeof(A));
   auto kern = small::jvp_kernel<T, A>;
   if constexpr (std::is_same<T, float>::value && std::is_same<A, float>::value)
@@ -239,14 +258,15 @@ int small_jvp(const void* q, const void* k, const void* v, const void* tq, const
   small_setup(kern, sm);
   kern<<<(unsigned)(s.B * s.H), small::NTHREADS, sm, st>>>(
       (const T*)q, (const T*)k, (const T*)v, (const T*)tq, (const T*)tk, (const T*)tv, lse,
-      (T*)o_tan, s);
+      (T*)o_tan, s, ly);
   return launch_status();
 }
 
 template <typename T, typename A = float>
 int small_hvp(const void* q, const void* k, const void* v, const void* w, const float* lse,
               const void* tq, const void* tk, const void* tv, void* hq, void* hk, void* hv,
-              void* o_tan, const Shape& s, cudaStream_t st) {
+              void* o_tan, const Shape& s, cudaStream_t st, const small::Layout* lyp = nullptr) {
+  const small::Layout ly = lyp ? *lyp : contiguous_layout(s);
   const size_t sm = small::smem_bytes((int)s.T, (int)s.M, (int)s.D, 3, 4, 4, sizeof(A));
   auto kern = small::hvp_kernel<T, A>;
   if constexpr (std::is_same<T, float>::value && std::is_same<A, float>::value)
@@ -254,7 +274,7 @@ int small_hvp(const void* q, const void* k, const void* v, const void* w, const 
   small_setup(kern, sm);
   kern<<<(unsigned)(s.B * s.H), small::NTHREADS, sm, st>>>(
       (const T*)q, (const T*)k, (const T*)v, (const T*)w, lse, (const T*)tq, (const T*)tk,
-      (const T*)tv, (T*)hq, (T*)hk, (T*)hv, (T*)o_tan, s);
+      (const T*)tv, (T*)hq, (T*)hk, (T*)hv, (T*)o_tan, s, ly);
   return launch_status();
 }
 
@@ -749,6 +769,98 @@ int theria_sdpa_bwd_noalloc(const void* q, const void* k, const void* v, const v
   return theria_sdpa_bwd(q, k, v, o, o_dtype, dout, lse, dq, dk, dv, scratch,
                          (int64_t)THERIA_NOALLOC_SCRATCH_BYTES, B, H, T, M, D, dtype, scale,
                          causal, stream);
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------ packed self-attention
+namespace {
+int qkv_check(int64_t B, int64_t H, int64_t T, int64_t D, int dtype) {
+  if (int e = check_shape(B, H, T, T, D, dtype)) return e;
+  Shape s{B, H, T, T, D, 1.f, 0};
+  if (!small_eligible(s)) return THERIA_ERR_UNSUPPORTED;
+  return THERIA_OK;
+}
+template <typename T>
+const T* part(const void* qkv, int which, int64_t H, int64_t D) {
+  return (const T*)qkv + which * H * D;
+}
+template <typename T>
+T* part(void* qkv, int which, int64_t H, int64_t D) {
+  return (T*)qkv + which * H * D;
+}
+template <typename T, typename A = float>
+int qkv_fwd(const void* qkv, void* o, float* lse, const Shape& s, cudaStream_t st) {
+  const small::Layout ly = packed_layout(s);
+  const int od = std::is_same<T, float>::value ? THERIA_F32
+                 : std::is_same<T, double>::value ? THERIA_F64 : -1;
+  return small_fwd<T, A>(part<T>(qkv, 0, s.H, s.D), part<T>(qkv, 1, s.H, s.D),
+                         part<T>(qkv, 2, s.H, s.D), o, od, lse, s, st, &ly);
+}
+template <typename T, typename A = float>
+int qkv_bwd(const void* qkv, const void* dout, const float* lse, void* dqkv, const Shape& s,
+            cudaStream_t st) {
+  const small::Layout ly = packed_layout(s);
+  return small_bwd<T, A>(part<T>(qkv, 0, s.H, s.D), part<T>(qkv, 1, s.H, s.D),
+                         part<T>(qkv, 2, s.H, s.D), dout, lse, part<T>(dqkv, 0, s.H, s.D),
+                         part<T>(dqkv, 1, s.H, s.D), part<T>(dqkv, 2, s.H, s.D), s, st, &ly);
+}
+template <typename T, typename A = float>
+int qkv_hvp(const void* qkv, const void* w, const float* lse, const void* tqkv, void* hqkv,
+            void* o_tan, const Shape& s, cudaStream_t st) {
+  const small::Layout ly = packed_layout(s);
+  T* h[3] = {nullptr, nullptr, nullptr};
+  if (hqkv)
+    for (int i = 0; i < 3; ++i) h[i] = part<T>(hqkv, i, s.H, s.D);
+  return small_hvp<T, A>(part<T>(qkv, 0, s.H, s.D), part<T>(qkv, 1, s.H, s.D),
+                         part<T>(qkv, 2, s.H, s.D), w, lse, part<T>(tqkv, 0, s.H, s.D),
+                         part<T>(tqkv, 1, s.H, s.D), part<T>(tqkv, 2, s.H, s.D), h[0], h[1],
+                         h[2], o_tan, s, st, &ly);
+}
+}  // namespace
+
+extern "C" {
+
+int theria_sdpa_qkv_fwd(const void* qkv, void* o, float* lse, int64_t B, int64_t H, int64_t T,
+                        int64_t D, int dtype, float scale, int causal, void* stream) {
+  if (int e = qkv_check(B, H, T, D, dtype)) return e;
+  if (empty_problem(B, H, T)) return THERIA_OK;
+  if (!qkv || !o || !lse) return THERIA_ERR_INVALID_ARG;
+  Shape s{B, H, T, T, D, scale, causal ? 1 : 0};
+  cudaStream_t st = (cudaStream_t)stream;
+  if (dtype == THERIA_F64)
+    return f64_fits(s, 1, 2, 1) ? qkv_fwd<double, double>(qkv, o, lse, s, st)
+                                : THERIA_ERR_UNSUPPORTED;
+  return THERIA_DISPATCH(dtype, qkv_fwd, qkv, o, lse, s, st);
+}
+
+int theria_sdpa_qkv_bwd(const void* qkv, const void* dout, const float* lse, void* dqkv,
+                        int64_t B, int64_t H, int64_t T, int64_t D, int dtype, float scale,
+                        int causal, void* stream) {
+  if (int e = qkv_check(B, H, T, D, dtype)) return e;
+  if (empty_problem(B, H, T)) return THERIA_OK;
+  if (!qkv || !dout || !lse || !dqkv) return THERIA_ERR_INVALID_ARG;
+  Shape s{B, H, T, T, D, scale, causal ? 1 : 0};
+  cudaStream_t st = (cudaStream_t)stream;
+  if (dtype == THERIA_F64)
+    return f64_fits(s, 2, 2, 2) ? qkv_bwd<double, double>(qkv, dout, lse, dqkv, s, st)
+                                : THERIA_ERR_UNSUPPORTED;
+  return THERIA_DISPATCH(dtype, qkv_bwd, qkv, dout, lse, dqkv, s, st);
+}
+
+int theria_sdpa_qkv_hvp(const void* qkv, const void* w, const float* lse, const void* tqkv,
+                        void* hqkv, void* o_tan, int64_t B, int64_t H, int64_t T, int64_t D,
+                        int dtype, float scale, int causal, void* stream) {
+  if (int e = qkv_check(B, H, T, D, dtype)) return e;
+  if (empty_problem(B, H, T)) return THERIA_OK;
+  if (!qkv || !w || !lse || !tqkv || (!hqkv && !o_tan)) return THERIA_ERR_INVALID_ARG;
+  Shape s{B, H, T, T, D, scale, causal ? 1 : 0};
+  cudaStream_t st = (cudaStream_t)stream;
+  if (dtype == THERIA_F64)
+    return f64_fits(s, 3, 4, 4)
+               ? qkv_hvp<double, double>(qkv, w, lse, tqkv, hqkv, o_tan, s, st)
+               : THERIA_ERR_UNSUPPORTED;
+  return THERIA_DISPATCH(dtype, qkv_hvp, qkv, w, lse, tqkv, hqkv, o_tan, s, st);
 }
 
 }  // extern "C"

@@ -23,6 +23,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from theria_b200.attention.fused import sdpa_fused
+from theria_b200.attention.packed import sdpa_qkv
 from theria_b200.maml.layer_norm import gelu, layer_norm
 from theria_b200.maml.task_bmm import add_bias, tbmm
 
@@ -101,10 +102,13 @@ class MAMLClassifier(nn.Module):
             p = lambda s: params[f"blocks.{i}.{s}"]  # noqa: E731
             a = _layer_norm(h, p("ln1_w"), p("ln1_b"))
             qkv = _linear(a, p("qkv_w"), p("qkv_b")).view(nt * n, L, 3, H, Dh)
-            qkv = qkv.permute(2, 0, 3, 1, 4)  # (3, nt*n, H, L, Dh)
-            q, k, v = qkv.unbind(0)  # one stack in the backward, not 3 scatters
-            o = self.attn_fn(q, k, v)  # (nt*n, H, L, Dh)
-            o = o.transpose(1, 2).reshape(nt, n, L, D)
+            if self.attn_fn is sdpa_fused and qkv.is_cuda:
+                # the default attention, on the packed projection: q, k, v
+                # read in place, O written token-major (no layout copies)
+                o = sdpa_qkv(qkv).reshape(nt, n, L, D)
+            else:
+                q, k, v = qkv.permute(2, 0, 3, 1, 4).unbind(0)  # (nt*n, H, L, Dh) each
+                o = self.attn_fn(q, k, v).transpose(1, 2).reshape(nt, n, L, D)
             h = h + _linear(o, p("out_w"), p("out_b"))
             f = _layer_norm(h, p("ln2_w"), p("ln2_b"))
             f = gelu(_linear(f, p("ff1_w"), p("ff1_b")))
