@@ -222,31 +222,28 @@ bwd2_kernel(const float* __restrict__ x, const float* __restrict__ w, int64_t ld
 }
 
 // out[t][s][d] = sum_cta ws[t][cta][s][d]  (NS * D values per task); out rows
-// for s = 0 .. NS-1 go to outs[s] (contiguous [nt][D]).  One CTA per task:
-// COLSUM_THREADS / (NS * D) groups of threads take interleaved CTAs, then
-// the groups' partials are added in a fixed order (deterministic).
+// for s = 0 .. NS-1 go to outs[s] (contiguous [nt][D]).  Grid (nt, NS*D/32):
+// lanes over 32 of the NS*D columns, 32 warps over interleaved CTAs, the
+// warps' partials added in a fixed order (deterministic).
 constexpr int COLSUM_THREADS = 1024;
 __global__ void __launch_bounds__(COLSUM_THREADS)
 colsum_kernel(const float* __restrict__ ws, float* __restrict__ out0,
               float* __restrict__ out1, int n_cta, int NS, int D) {
-  __shared__ float part[COLSUM_THREADS];
+  __shared__ float part[COLSUM_THREADS / 32][33];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t t = blockIdx.x;
-  const int W = NS * D;
-  const int groups = max(1, COLSUM_THREADS / W);
-  for (int e0 = 0; e0 < W; e0 += COLSUM_THREADS) {
-    const int g = threadIdx.x / W, e = e0 + threadIdx.x % W;
-    float v = 0.f;
-    if (g < groups && e < W)
-      for (int k = g; k < n_cta; k += groups) v += ws[((t * n_cta) + k) * W + e];
-    part[threadIdx.x] = v;
-    __syncthreads();
-    if (threadIdx.x < W && e0 + threadIdx.x < W) {
-      float s = 0.f;
-      for (int gg = 0; gg < groups; ++gg) s += part[gg * W + threadIdx.x];
-      const int ee = e0 + threadIdx.x, sidx = ee / D, d = ee - sidx * D;
-      (sidx == 0 ? out0 : out1)[t * D + d] = s;
-    }
-    __syncthreads();
+  const int W = NS * D, e = blockIdx.y * 32 + lane;
+  float v = 0.f;
+  if (e < W)
+    for (int k = warp; k < n_cta; k += COLSUM_THREADS / 32) v += ws[((t * n_cta) + k) * W + e];
+  part[warp][lane] = v;
+  __syncthreads();
+  if (warp == 0 && e < W) {
+    float sum = 0.f;
+#pragma unroll 8
+    for (int w = 0; w < COLSUM_THREADS / 32; ++w) sum += part[w][lane];
+    const int si = e / D, d = e - si * D;
+    (si == 0 ? out0 : out1)[t * D + d] = sum;
   }
 }
 

@@ -901,7 +901,8 @@ struct LnBwd {
     dim3 grid((unsigned)ln_ctas(R), (unsigned)nt);
     ln::bwd_kernel<V><<<grid, ln::WARPS * 32, 0, st>>>(x, w, ldw, gy, gx, ws, R, D, eps);
     if (int e = launch_status()) return e;
-    ln::colsum_kernel<<<(unsigned)nt, ln::COLSUM_THREADS, 0, st>>>(ws, gw, gb, (int)grid.x, 2, D);
+    ln::colsum_kernel<<<dim3((unsigned)nt, (unsigned)((2 * D + 31) / 32)), ln::COLSUM_THREADS, 0, st>>>(
+        ws, gw, gb, (int)grid.x, 2, D);
     return launch_status();
   }
 };
@@ -914,7 +915,8 @@ struct LnBwd2 {
     ln::bwd2_kernel<V><<<grid, ln::WARPS * 32, 0, st>>>(x, w, ldw, gy, u, a, c, dx, dgy, ws,
                                                        R, D, eps);
     if (int e = launch_status()) return e;
-    ln::colsum_kernel<<<(unsigned)nt, ln::COLSUM_THREADS, 0, st>>>(ws, dw, dw, (int)grid.x, 1, D);
+    ln::colsum_kernel<<<dim3((unsigned)nt, (unsigned)((D + 31) / 32)), ln::COLSUM_THREADS, 0, st>>>(
+        ws, dw, dw, (int)grid.x, 1, D);
     return launch_status();
   }
 };
@@ -984,8 +986,8 @@ int theria_rowsum(const float* x, float* out, void* workspace, int64_t workspace
   dim3 grid((unsigned)nt, (unsigned)((C + 31) / 32), (unsigned)chunks);
   ln::rowsum_partial_kernel<<<grid, ln::WARPS * 32, 0, st>>>(x, ws, R, (int)C);
   if (int e = launch_status()) return e;
-  ln::colsum_kernel<<<(unsigned)nt, ln::COLSUM_THREADS, 0, st>>>(ws, out, out, (int)chunks, 1,
-                                                                 (int)C);
+  ln::colsum_kernel<<<dim3((unsigned)nt, (unsigned)((C + 31) / 32)), ln::COLSUM_THREADS, 0, st>>>(
+      ws, out, out, (int)chunks, 1, (int)C);
   return launch_status();
 }
 
