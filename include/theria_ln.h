@@ -53,6 +53,16 @@ int64_t theria_rowsum_workspace_bytes(int64_t nt, int64_t R, int64_t C);
 int theria_rowsum(const float* x, float* out, void* workspace, int64_t workspace_bytes,
                   int64_t nt, int64_t R, int64_t C, void* stream);
 
+/* out = x + b (broadcast over rows) [+ res]: x, res, out [nt, R, C] float32
+ * contiguous, b rows at stride ldb (0: shared); res may be NULL. */
+int theria_add_bias(const float* x, const float* b, int64_t ldb, const float* res, float* out,
+                    int64_t nt, int64_t R, int64_t C, void* stream);
+
+/* out[t][e] = sum_c x[t][c][e] for x [nt, S, W] float32 contiguous (the
+ * partial products of the model's split long-row matmuls); deterministic. */
+int theria_chunk_sum(const float* x, float* out, int64_t nt, int64_t S, int64_t W,
+                     void* stream);
+
 /* Second derivative of the exact GELU through its backward gx = gy *
  * gelu'(x): for a cotangent u of gx, dgy = u * gelu'(x) and
  * dx = u * gy * gelu''(x); x, gy, u, dx, dgy hold n float32 each. */

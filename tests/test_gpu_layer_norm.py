@@ -87,20 +87,24 @@ def test_task_linear_first_and_second_derivatives():
     r0 = torch.randn(3, 1600, 70, generator=g)
     v0 = torch.randn(3, 1600, 64, generator=g)
 
+    res0 = torch.randn(3, 1600, 70, generator=g)
+
     def run(lin, dev, dt):
         h = h0.to(dev, dt).requires_grad_(True)
         flat = flat0.to(dev, dt).requires_grad_(True)
+        res = res0.to(dev, dt).requires_grad_(True)
         w = flat[:, :70 * 64].view(3, 70, 64)
         b = flat[:, 70 * 64 + 30:]
-        y = lin(h, w, b)
-        gh, gflat = torch.autograd.grad((y.square() * r0.to(dev, dt)).sum(), (h, flat),
-                                        create_graph=True)
-        l2 = (gh * v0.to(dev, dt)).sum() + gflat.square().sum()
-        return (y, gh, gflat) + torch.autograd.grad(l2, (h, flat))
+        y = lin(h, w, b, res)
+        gh, gflat, gres = torch.autograd.grad((y.square() * r0.to(dev, dt)).sum(),
+                                              (h, flat, res), create_graph=True)
+        l2 = (gh * v0.to(dev, dt)).sum() + gflat.square().sum() + gres.square().sum()
+        return (y, gh, gflat, gres) + torch.autograd.grad(l2, (h, flat, res))
 
-    got = run(lambda h, w, b: add_bias(tbmm(h, w.transpose(1, 2)), b), "cuda", torch.float32)
-    ref = run(lambda h, w, b: torch.bmm(h, w.transpose(1, 2)) + b.unsqueeze(1), "cpu",
-              torch.float64)
+    got = run(lambda h, w, b, res: add_bias(tbmm(h, w.transpose(1, 2)), b, res), "cuda",
+              torch.float32)
+    ref = run(lambda h, w, b, res: res + torch.bmm(h, w.transpose(1, 2)) + b.unsqueeze(1),
+              "cpu", torch.float64)
     for a, b in zip(got, ref):
         assert _rel(a, b) <= 1e-5
 

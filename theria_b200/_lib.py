@@ -55,6 +55,8 @@ SIGNATURES = {
     "theria_ln_workspace_bytes": (_i64, [_i64] * 3),
     "theria_rowsum_workspace_bytes": (_i64, [_i64] * 3),
     "theria_gelu_bwd2": (_i, [_vp] * 5 + [_i64, _vp]),
+    "theria_chunk_sum": (_i, [_vp, _vp, _i64, _i64, _i64, _vp]),
+    "theria_add_bias": (_i, [_vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _vp]),
     "theria_rowsum": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp]),
     "theria_ln_fwd": (_i, [_vp, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _f, _vp]),
     "theria_ln_bwd": (_i, [_vp, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _i64,

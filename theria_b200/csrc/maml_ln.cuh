@@ -296,5 +296,34 @@ __global__ void gelu_bwd2_kernel(const float* __restrict__ x, const float* __res
   }
 }
 
+// out[t][e] = sum_c x[t][c][e] for x [nt, S, W] (the S partial products of a
+// split reduction): one thread per output element, chunks added in order.
+__global__ void chunk_sum_kernel(const float* __restrict__ x, float* __restrict__ out,
+                                 int64_t nt, int S, int64_t W) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nt * W;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = i / W, e = i - t * W;
+    const float* p = x + t * S * W + e;
+    float v = 0.f;
+    for (int c = 0; c < S; ++c) v += p[c * W];
+    out[i] = v;
+  }
+}
+
+// out[t][r][c] = x[t][r][c] + b[t][c] (+ res[t][r][c]) for x, res, out
+// [nt, R, C] contiguous and b rows at stride ldb (0: one row for all tasks).
+__global__ void add_bias_kernel(const float* __restrict__ x, const float* __restrict__ b,
+                                int64_t ldb, const float* __restrict__ res,
+                                float* __restrict__ out, int64_t nt, int64_t R, int64_t C) {
+  const int64_t n = nt * R * C;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = i / (R * C), c = i % C;
+    float v = x[i] + b[t * ldb + c];
+    if (res) v += res[i];
+    out[i] = v;
+  }
+}
+
 }  // namespace ln
 }  // namespace theria

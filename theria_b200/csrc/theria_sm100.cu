@@ -953,6 +953,31 @@ int theria_ln_bwd(const float* x, const float* w, int64_t ldw, const float* gy, 
                             eps, (cudaStream_t)stream);
 }
 
+int theria_add_bias(const float* x, const float* b, int64_t ldb, const float* res, float* out,
+                    int64_t nt, int64_t R, int64_t C, void* stream) {
+  if (nt < 0 || R < 0 || C <= 0 || (ldb < C && ldb != 0)) return THERIA_ERR_INVALID_ARG;
+  if (nt == 0 || R == 0) return THERIA_OK;
+  if (!x || !b || !out) return THERIA_ERR_INVALID_ARG;
+  const int64_t blocks = std::min<int64_t>((nt * R * C + 255) / 256, 148 * 16);
+  ln::add_bias_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(x, b, ldb, res, out, nt,
+                                                                           R, C);
+  return launch_status();
+}
+
+int theria_chunk_sum(const float* x, float* out, int64_t nt, int64_t S, int64_t W,
+                     void* stream) {
+  if (nt < 0 || S < 0 || W < 0 || S > 65535) return THERIA_ERR_INVALID_ARG;
+  if (nt == 0 || W == 0) return THERIA_OK;
+  if (!x || !out) return THERIA_ERR_INVALID_ARG;
+  if (S == 0) {
+    cudaMemsetAsync(out, 0, nt * W * sizeof(float), (cudaStream_t)stream);
+    return THERIA_OK;
+  }
+  const int64_t blocks = std::min<int64_t>((nt * W + 255) / 256, 148 * 16);
+  ln::chunk_sum_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(x, out, nt, (int)S, W);
+  return launch_status();
+}
+
 int theria_gelu_bwd2(const float* x, const float* gy, const float* u, float* dx, float* dgy,
                      int64_t n, void* stream) {
   if (n < 0) return THERIA_ERR_INVALID_ARG;

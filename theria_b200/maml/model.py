@@ -39,12 +39,13 @@ class ModelConfig:
     n_classes: int = 5
 
 
-def _linear(h, w, b):
-    # h (nt, ..., din), w (nt, dout, din), b (nt, dout).  tbmm: the weight
-    # gradients reduce over all rows of a task, which tbmm splits.
+def _linear(h, w, b, res=None):
+    # h (nt, ..., din), w (nt, dout, din), b (nt, dout); res: an optional
+    # residual added in the bias kernel.  tbmm: the weight gradients reduce
+    # over all rows of a task, which tbmm splits.
     nt = h.shape[0]
     shp = h.shape
-    out = add_bias(tbmm(h.reshape(nt, -1, shp[-1]), w.transpose(1, 2)), b)
+    out = add_bias(tbmm(h.reshape(nt, -1, shp[-1]), w.transpose(1, 2)), b, res)
     return out.view(*shp[:-1], w.shape[1])
 
 
@@ -109,10 +110,10 @@ class MAMLClassifier(nn.Module):
             else:
                 q, k, v = qkv.permute(2, 0, 3, 1, 4).unbind(0)  # (nt*n, H, L, Dh) each
                 o = self.attn_fn(q, k, v).transpose(1, 2).reshape(nt, n, L, D)
-            h = h + _linear(o, p("out_w"), p("out_b"))
+            h = _linear(o, p("out_w"), p("out_b"), res=h)
             f = _layer_norm(h, p("ln2_w"), p("ln2_b"))
             f = gelu(_linear(f, p("ff1_w"), p("ff1_b")))
-            h = h + _linear(f, p("ff2_w"), p("ff2_b"))
+            h = _linear(f, p("ff2_w"), p("ff2_b"), res=h)
         h = _layer_norm(h, params["lnf_w"], params["lnf_b"]).mean(dim=2)  # (nt, n, D)
         return _linear(h, params["head_w"], params["head_b"])  # (nt, n, C)
 

@@ -52,7 +52,13 @@ def _bmm(a, b):
         return torch.bmm(a, b)
     at = a.transpose(1, 2).reshape(n * s, k // s, m).transpose(1, 2)
     bt = b.reshape(n * s, k // s, p)
-    return torch.bmm(at, bt).view(n, s, m, p).sum(1)
+    part = torch.bmm(at, bt)  # [n * s, m, p]
+    if not (part.is_cuda and part.dtype == torch.float32):
+        return part.view(n, s, m, p).sum(1)
+    out = torch.empty(n, m, p, dtype=part.dtype, device=part.device)
+    _lib.check(_lib.load().theria_chunk_sum(_lib.ptr(part), _lib.ptr(out), n, s, m * p,
+                                            _lib.stream_of(part)), "theria_chunk_sum")
+    return out
 
 
 class _TaskBmm(torch.autograd.Function):
@@ -105,24 +111,37 @@ class _RowSum(torch.autograd.Function):
 
 
 class _AddBias(torch.autograd.Function):
-    """x [n, R, C] + b [n, C] broadcast over R; the bias gradient is a
-    row sum (differentiable: its backward is a broadcast)."""
+    """x [n, R, C] + b [n, C] broadcast over R (+ an optional residual of x's
+    shape, added in the same kernel); the bias gradient is a row sum
+    (differentiable: its backward is a broadcast)."""
 
     @staticmethod
-    def forward(ctx, x, b):
-        return x + b.unsqueeze(1)
+    def forward(ctx, x, b, res):
+        ctx.has_res = res is not None
+        x = x.contiguous()
+        res = None if res is None else res.contiguous()
+        if b.stride(1) != 1:
+            b = b.contiguous()
+        n, r, c = x.shape
+        out = torch.empty_like(x)
+        _lib.check(_lib.load().theria_add_bias(
+            _lib.ptr(x), _lib.ptr(b), b.stride(0), _lib.ptr(res), _lib.ptr(out), n, r, c,
+            _lib.stream_of(x)), "theria_add_bias")
+        return out
 
     @staticmethod
     def backward(ctx, g):
         gb = _RowSum.apply(g) if ctx.needs_input_grad[1] else None
-        return g, gb
+        return g, gb, (g if ctx.has_res else None)
 
 
-def add_bias(x, b):
-    """``x + b[:, None, :]`` for x [n, R, C] float32 with a fused bias gradient."""
+def add_bias(x, b, res=None):
+    """``[res +] x + b[:, None, :]`` for x [n, R, C] float32, with a fused
+    bias gradient."""
     if x.dtype != torch.float32 or not x.is_cuda:
-        return x + b.unsqueeze(1)
-    return _AddBias.apply(x, b)
+        out = x + b.unsqueeze(1)
+        return out if res is None else res.reshape(out.shape) + out
+    return _AddBias.apply(x, b, None if res is None else res.reshape(x.shape))
 
 
 __all__ = ["tbmm", "add_bias"]
