@@ -102,3 +102,19 @@ def test_task_sharded_allreduce_matches_single_process(tmp_path):
     step.loss_and_grad(stack_tasks(sample_tasks(3, 4, TaskConfig(seq_len=16))))
     g1 = step.bucket
     assert (g1 - g2).abs().max().item() <= 1e-5 * g1.abs().max().item()
+
+
+def test_task_bmm_split_reduction_and_its_derivatives():
+    # tbmm splits a long reduction into batch entries (views) and adds the
+    # partials; equal to bmm, and differentiable twice through its own
+    # backward (which calls tbmm again), for row-major and transposed inputs
+    from theria_b200.maml.task_bmm import _split, tbmm
+    assert _split(4, 64, 1600, 256) == 8 and _split(32, 64, 1600, 256) == 2
+    g = torch.Generator().manual_seed(0)
+    a = torch.randn(2, 3, 512, generator=g, dtype=torch.float64, requires_grad=True)
+    b = torch.randn(2, 512, 5, generator=g, dtype=torch.float64, requires_grad=True)
+    assert _split(2, 3, 512, 5) > 1
+    assert torch.allclose(tbmm(a, b), torch.bmm(a, b))
+    assert torch.autograd.gradgradcheck(tbmm, (a, b))
+    at = torch.randn(2, 512, 3, generator=g, dtype=torch.float64, requires_grad=True)
+    assert torch.autograd.gradgradcheck(lambda x, y: tbmm(x.transpose(1, 2), y), (at, b))
