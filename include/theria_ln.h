@@ -4,7 +4,7 @@
  *
  * x, y, gy, gx, u, dx, dgy are [nt, R, D] float32, contiguous; w, b are
  * [nt, D] float32 with row stride ldw (elements; 0 = one row shared by
- * all tasks); gw, gb, a, c, dw are
+ * all tasks); a, c have row strides lda, ldc the same way; gw, gb, dw are
  * [nt, D] contiguous.  eps is added to the variance (as torch layer_norm).
  *   forward      y  = (x - mean) * rstd * w + b
  *   backward     gx = rstd * P(gy * w), gw = sum_rows gy * xhat, gb = sum_rows gy
@@ -41,10 +41,11 @@ int theria_ln_bwd(const float* x, const float* w, int64_t ldw, const float* gy, 
                   float* gw, float* gb, void* workspace, int64_t workspace_bytes,
                   int64_t nt, int64_t R, int64_t D, float eps, void* stream);
 
+/* a, c: rows at strides lda, ldc (like ldw) */
 int theria_ln_bwd2(const float* x, const float* w, int64_t ldw, const float* gy,
-                   const float* u, const float* a, const float* c, float* dx, float* dw,
-                   float* dgy, void* workspace, int64_t workspace_bytes, int64_t nt,
-                   int64_t R, int64_t D, float eps, void* stream);
+                   const float* u, const float* a, int64_t lda, const float* c, int64_t ldc,
+                   float* dx, float* dw, float* dgy, void* workspace, int64_t workspace_bytes,
+                   int64_t nt, int64_t R, int64_t D, float eps, void* stream);
 
 /* out[t][c] = sum_r x[t][r][c] for x [nt, R, C] float32 contiguous (the
  * bias gradient of the model's task-batched linears), C <= 1024, through a

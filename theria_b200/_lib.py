@@ -61,8 +61,8 @@ SIGNATURES = {
     "theria_ln_fwd": (_i, [_vp, _vp, _vp, _i64, _vp, _i64, _i64, _i64, _f, _vp]),
     "theria_ln_bwd": (_i, [_vp, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _i64,
                            _i64, _i64, _i64, _f, _vp]),
-    "theria_ln_bwd2": (_i, [_vp, _vp, _i64] + [_vp] * 7 + [_vp, _i64, _i64, _i64, _i64, _f,
-                                                         _vp]),
+    "theria_ln_bwd2": (_i, [_vp, _vp, _i64, _vp, _vp, _vp, _i64, _vp, _i64, _vp, _vp, _vp,
+                            _vp, _i64, _i64, _i64, _i64, _f, _vp]),
     "theria_get_device_error": (_i, [ctypes.POINTER(ctypes.c_int), _vp]),
     "theria_clear_device_error": (_i, [_vp]),
 }

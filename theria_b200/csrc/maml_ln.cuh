@@ -163,16 +163,16 @@ template <int V>
 __global__ void __launch_bounds__(WARPS * 32)
 bwd2_kernel(const float* __restrict__ x, const float* __restrict__ w, int64_t ldw,
             const float* __restrict__ gy, const float* __restrict__ u,
-            const float* __restrict__ a, const float* __restrict__ c,
-            float* __restrict__ dx, float* __restrict__ dgy, float* __restrict__ ws, int64_t R,
+            const float* __restrict__ a, int64_t lda, const float* __restrict__ c,
+            int64_t ldc, float* __restrict__ dx, float* __restrict__ dgy, float* __restrict__ ws, int64_t R,
             int D, float eps) {
   __shared__ float smem[WARPS * 32 * V];
   const int warp = threadIdx.x >> 5;
   const int64_t t = blockIdx.y;
   float wr[V], ar[V], cr[V];
   load_row(wr, w + t * ldw, D);
-  load_row(ar, a ? a + t * D : nullptr, D);
-  load_row(cr, c ? c + t * D : nullptr, D);
+  load_row(ar, a ? a + t * lda : nullptr, D);
+  load_row(cr, c ? c + t * ldc : nullptr, D);
   float acc[1][V];
 #pragma unroll
   for (int i = 0; i < V; ++i) acc[0][i] = 0.f;

@@ -909,11 +909,12 @@ struct LnBwd {
 template <int V>
 struct LnBwd2 {
   static int run(const float* x, const float* w, int64_t ldw, const float* gy, const float* u,
-                 const float* a, const float* c, float* dx, float* dw, float* dgy, float* ws,
-                 int64_t nt, int64_t R, int D, float eps, cudaStream_t st) {
+                 const float* a, int64_t lda, const float* c, int64_t ldc, float* dx, float* dw,
+                 float* dgy, float* ws, int64_t nt, int64_t R, int D, float eps,
+                 cudaStream_t st) {
     dim3 grid((unsigned)ln_ctas(R), (unsigned)nt);
-    ln::bwd2_kernel<V><<<grid, ln::WARPS * 32, 0, st>>>(x, w, ldw, gy, u, a, c, dx, dgy, ws,
-                                                       R, D, eps);
+    ln::bwd2_kernel<V><<<grid, ln::WARPS * 32, 0, st>>>(x, w, ldw, gy, u, a, lda, c, ldc, dx,
+                                                       dgy, ws, R, D, eps);
     if (int e = launch_status()) return e;
     ln::colsum_kernel<<<dim3((unsigned)nt, (unsigned)((D + 31) / 32)), ln::COLSUM_THREADS, 0, st>>>(
         ws, dw, dw, (int)grid.x, 1, D);
@@ -1017,10 +1018,11 @@ int theria_rowsum(const float* x, float* out, void* workspace, int64_t workspace
 }
 
 int theria_ln_bwd2(const float* x, const float* w, int64_t ldw, const float* gy,
-                   const float* u, const float* a, const float* c, float* dx, float* dw,
-                   float* dgy, void* workspace, int64_t workspace_bytes, int64_t nt,
-                   int64_t R, int64_t D, float eps, void* stream) {
+                   const float* u, const float* a, int64_t lda, const float* c, int64_t ldc,
+                   float* dx, float* dw, float* dgy, void* workspace, int64_t workspace_bytes,
+                   int64_t nt, int64_t R, int64_t D, float eps, void* stream) {
   if (int e = ln_check(nt, R, D, ldw)) return e;
+  if ((a && lda < D && lda != 0) || (c && ldc < D && ldc != 0)) return THERIA_ERR_INVALID_ARG;
   if (nt == 0) return THERIA_OK;
   if (!x || !w || !gy || !dx || !dw || !dgy) return THERIA_ERR_INVALID_ARG;
   if (R == 0) {
@@ -1029,8 +1031,8 @@ int theria_ln_bwd2(const float* x, const float* w, int64_t ldw, const float* gy,
   }
   if (!workspace || workspace_bytes < theria_ln_workspace_bytes(nt, R, D))
     return THERIA_ERR_WORKSPACE;
-  return ln_dispatch<LnBwd2>(D, x, w, ldw, gy, u, a, c, dx, dw, dgy, (float*)workspace, nt, R,
-                             (int)D, eps, (cudaStream_t)stream);
+  return ln_dispatch<LnBwd2>(D, x, w, ldw, gy, u, a, lda, c, ldc, dx, dw, dgy,
+                             (float*)workspace, nt, R, (int)D, eps, (cudaStream_t)stream);
 }
 
 }  // extern "C"

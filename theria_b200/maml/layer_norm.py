@@ -36,6 +36,13 @@ def _ldw(w):
     return w.stride(0)
 
 
+def _rowwise(t):
+    # [nt, D] with unit column stride (rows may be strided views of a flat
+    # per-task buffer); anything else is packed
+    return t if t.stride(1) == 1 and (t.stride(0) >= t.shape[1] or t.stride(0) == 0) \
+        else t.contiguous()
+
+
 def _ws(nt, R, D, like):
     n = _lib.load().theria_ln_workspace_bytes(nt, R, D)
     return torch.empty(max(n, 4) // 4, dtype=torch.float32, device=like.device)
@@ -65,15 +72,16 @@ class _LayerNormBackward(torch.autograd.Function):
         x, w, gy = ctx.saved_tensors
         nt, R, D = _rows(x, w)
         u = None if u is None else u.contiguous()
-        a = None if a is None else a.contiguous()
-        c = None if c is None else c.contiguous()
+        a = None if a is None else _rowwise(a)
+        c = None if c is None else _rowwise(c)
         dx = torch.empty_like(x)
         dgy = torch.empty_like(x)
         dw = torch.empty(nt, D, dtype=x.dtype, device=x.device)
         ws = _ws(nt, R, D, x)
         _lib.check(_lib.load().theria_ln_bwd2(
             _lib.ptr(x), _lib.ptr(w), _ldw(w), _lib.ptr(gy), _lib.ptr(u), _lib.ptr(a),
-            _lib.ptr(c), _lib.ptr(dx), _lib.ptr(dw), _lib.ptr(dgy), _lib.ptr(ws),
+            0 if a is None else a.stride(0), _lib.ptr(c), 0 if c is None else c.stride(0),
+            _lib.ptr(dx), _lib.ptr(dw), _lib.ptr(dgy), _lib.ptr(ws),
             ws.numel() * 4, nt, R, D, EPS, _lib.stream_of(x)), "theria_ln_bwd2")
         return dx, dw, dgy
 
