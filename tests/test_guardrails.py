@@ -65,3 +65,16 @@ def test_no_cpu_fallback_for_fused_backend():
     q, k, v = _cpu()
     with pytest.raises(AssertionError, match="requires CUDA"):
         sdpa_custom(q, k, v, backend="triton_full_fused")
+
+
+def test_packed_attention_and_layer_norm_refuse_cpu_tensors_loudly():
+    # the packed attention has no CPU path; the MAML LayerNorm / GELU use the
+    # composed torch form only for CPU tensors (the CPU model of the tests)
+    import torch.nn.functional as F
+    from theria_b200.attention.packed import sdpa_qkv
+    from theria_b200.maml.layer_norm import gelu, layer_norm, layer_norm_reference
+    with pytest.raises(AssertionError, match="CUDA"):
+        sdpa_qkv(torch.randn(1, 4, 3, 2, 8))
+    x, w, b = torch.randn(2, 5, 16), torch.rand(2, 16) + 0.5, torch.randn(2, 16)
+    assert torch.allclose(layer_norm(x, w, b), layer_norm_reference(x, w, b))
+    assert torch.allclose(gelu(x), F.gelu(x))

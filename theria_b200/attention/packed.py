@@ -8,7 +8,7 @@ from the projection and write O, dqkv and the HVP's hqkv in these layouts
 (``theria_sdpa_qkv_*`` in ``include/theria_sdpa.h``), so the transposes and
 packing copies around the attention disappear from the forward, the
 backward and the double backward.  It serves T <= 64 and D <= 64; other
-shapes take the general path (the same kernels families through
+shapes take the general path (the same kernel families through
 ``sdpa_fused`` on unpacked heads).
 """
 
