@@ -100,3 +100,34 @@ def test_layer_norm_arguments_checked_on_the_host():
     assert lib.theria_ln_bwd(p, p, 64, p, p, p, p, None, 0, 4, 100, 64, 1e-5, None) == \
         _lib.THERIA_ERR_WORKSPACE
     assert lib.theria_ln_workspace_bytes(4, 100, 64) == 4 * 7 * 2 * 64 * 4  # ceil(100 / 16) CTAs
+
+
+def test_packed_attention_arguments_checked_on_the_host():
+    lib = _lib.load()
+    p = ctypes.c_void_p(16)
+    # beyond the whole-head kernels (T or D > 64): unsupported, not rerouted
+    assert lib.theria_sdpa_qkv_fwd(p, p, p, 2, 4, 65, 16, 0, 0.25, 0, None) == \
+        _lib.THERIA_ERR_UNSUPPORTED
+    assert lib.theria_sdpa_qkv_bwd(p, p, p, p, 2, 4, 64, 96, 0, 0.25, 0, None) in \
+        (_lib.THERIA_ERR_UNSUPPORTED, _lib.THERIA_ERR_INVALID_ARG)
+    assert lib.theria_sdpa_qkv_fwd(None, p, p, 2, 4, 64, 16, 0, 0.25, 0, None) == \
+        _lib.THERIA_ERR_INVALID_ARG
+    # the HVP needs at least one output
+    assert lib.theria_sdpa_qkv_hvp(p, p, p, p, None, None, 2, 4, 64, 16, 0, 0.25, 0, None) == \
+        _lib.THERIA_ERR_INVALID_ARG
+    assert lib.theria_sdpa_qkv_fwd(p, p, p, 0, 4, 64, 16, 0, 0.25, 0, None) == _lib.THERIA_OK
+
+
+def test_maml_helper_arguments_checked_on_the_host():
+    lib = _lib.load()
+    p = ctypes.c_void_p(16)
+    assert lib.theria_rowsum(p, p, None, 0, 4, 100, 64, None) == _lib.THERIA_ERR_WORKSPACE
+    assert lib.theria_rowsum(p, p, p, 1 << 20, 4, 100, 2048, None) == _lib.THERIA_ERR_UNSUPPORTED
+    assert lib.theria_rowsum_workspace_bytes(4, 300, 64) == 4 * 3 * 64 * 4
+    assert lib.theria_add_bias(p, p, 32, None, p, 4, 10, 64, None) == \
+        _lib.THERIA_ERR_INVALID_ARG  # ldb < C
+    assert lib.theria_chunk_sum(None, p, 4, 8, 100, None) == _lib.THERIA_ERR_INVALID_ARG
+    assert lib.theria_gelu_bwd2(p, p, None, p, p, 10, None) == _lib.THERIA_ERR_INVALID_ARG
+    assert lib.theria_gelu_bwd2(None, None, None, None, None, 0, None) == _lib.THERIA_OK
+    assert lib.theria_ln_bwd2(p, p, 64, p, p, p, 8, p, 64, p, p, p, p, 1 << 20, 4, 100, 64,
+                              1e-5, None) == _lib.THERIA_ERR_INVALID_ARG  # lda < D
