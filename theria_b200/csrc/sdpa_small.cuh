@@ -405,6 +405,22 @@ jvp_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
 
 // ---------------------------------------------------------------- HVP
 // Full HVP of L = <O, W> along (tQ, tK, tV): hQ, hK, hV and Odot.
+//
+// Shared memory is used in phases so that a MAML head (T = M = 64, D = 16,
+// fp32) needs 74 KB and three CTAs fit per SM: never more than the four
+// score-shaped matrices plus two operand matrices are resident.
+//   R0 = [P | Pdot]          (first Q, tQ, K, tK are read from R1 instead)
+//   R1 = [dP->dS | dPd->dSd] (holds Q, tQ, K, tK until S and Sdot exist)
+//   OP0, OP1 = W and V, then W and tV, then V and tV
+// and Q, tQ, K, tK are read again from global memory (L2) into R0 once P
+// and Pdot are no longer needed.
+inline size_t hvp_smem_bytes(int T, int M, int D, size_t elem) {
+  const size_t ssz = (size_t)T * (M + 1), opq = (size_t)T * (D + 1), opk = (size_t)M * (D + 1);
+  const size_t half = 2 * ssz > 2 * (opq + opk) ? 2 * ssz : 2 * (opq + opk);
+  const size_t slot = opq > opk ? opq : opk;
+  return elem * (2 * half + 2 * slot + (size_t)T);
+}
+
 template <typename T, typename A = float, int NC = 0, int DC = 0>
 __global__ void __launch_bounds__(NTHREADS)
 hvp_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
@@ -419,32 +435,42 @@ hvp_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
   const int64_t bh = blockIdx.x, hb = bh / s.H, hh = bh - hb * s.H;
   const int64_t qo = hb * ly.qb + hh * ly.qh, ko = hb * ly.kb + hh * ly.kh,
                 oo = hb * ly.ob + hh * ly.oh;
-  const int qsz = Tq * (D + 1), ksz = M * (D + 1), ssz = Tq * lm;
-  A* Q = sm;
-  A* TQ = Q + qsz;
-  A* W = TQ + qsz;
-  A* K = W + qsz;
-  A* TK = K + ksz;
-  A* V = TK + ksz;
-  A* TV = V + ksz;
-  A* P = TV + ksz;
-  A* PD = P + ssz;   // Sdot -> Pdot
-  A* DS = PD + ssz;  // dP   -> dS
-  A* DSD = DS + ssz; // dPd  -> dSd
-  A* L = DSD + ssz;
-  load_mat(Q, q + qo, Tq, D, ly.qt);
-  load_mat(TQ, tq + qo, Tq, D, ly.qt);
-  load_mat(W, w + oo, Tq, D, ly.ot);
-  load_mat(K, k + ko, M, D, ly.kt);
-  load_mat(TK, tk + ko, M, D, ly.kt);
-  load_mat(V, v + ko, M, D, ly.kt);
-  load_mat(TV, tv + ko, M, D, ly.kt);
+  const int ssz = Tq * lm, opq = Tq * (D + 1), opk = M * (D + 1);
+  const int half = 2 * ssz > 2 * (opq + opk) ? 2 * ssz : 2 * (opq + opk);
+  const int slot = opq > opk ? opq : opk;
+  A* R0 = sm;
+  A* R1 = R0 + half;
+  A* OP0 = R1 + half;
+  A* OP1 = OP0 + slot;
+  A* L = OP1 + slot;
+  A* P = R0;
+  A* PD = R0 + ssz;   // Sdot -> Pdot
+  A* DS = R1;         // dP   -> dS
+  A* DSD = R1 + ssz;  // dPd  -> dSd
+  auto load_qk = [&](A* base) {  // Q, tQ, K, tK packed at base
+    load_mat(base, q + qo, Tq, D, ly.qt);
+    load_mat(base + opq, tq + qo, Tq, D, ly.qt);
+    load_mat(base + 2 * opq, k + ko, M, D, ly.kt);
+    load_mat(base + 2 * opq + opk, tk + ko, M, D, ly.kt);
+  };
+  // S and Sdot from Q, tQ, K, tK held in R1
+  load_qk(R1);
+  load_mat(OP0, w + oo, Tq, D, ly.ot);
+  load_mat(OP1, v + ko, M, D, ly.kt);
   for (int i = threadIdx.x; i < Tq; i += blockDim.x) L[i] = lse[bh * Tq + i];
   __syncthreads();
-  abt(P, lm, Q, K, Tq, M, D, A(s.scale));
-  abt2(PD, lm, TQ, K, Q, TK, Tq, M, D, A(s.scale));
-  abt(DS, lm, W, V, Tq, M, D, A(1));
-  abt(DSD, lm, W, TV, Tq, M, D, A(1));
+  {
+    const A *Q = R1, *TQ = R1 + opq, *K = R1 + 2 * opq, *TK = K + opk;
+    abt(P, lm, Q, K, Tq, M, D, A(s.scale));
+    abt2(PD, lm, TQ, K, Q, TK, Tq, M, D, A(s.scale));
+  }
+  __syncthreads();
+  // dP = W V^T over the dead Q/K copies, then dPd = W tV^T
+  abt(DS, lm, OP0, OP1, Tq, M, D, A(1));
+  __syncthreads();
+  load_mat(OP1, tv + ko, M, D, ly.kt);
+  __syncthreads();
+  abt(DSD, lm, OP0, OP1, Tq, M, D, A(1));
   __syncthreads();
   exact_lse(P, lm, L, Tq, M, s.causal);
   __syncthreads();
@@ -475,10 +501,21 @@ hvp_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict
     }
   }
   __syncthreads();
-  if (hq) sx2(hq + qo, ly.qt, DSD, K, DS, TK, lm, Tq, M, D, A(s.scale));
-  if (hk) stx2(hk + ko, ly.kt, DSD, Q, DS, TQ, lm, Tq, M, D, A(s.scale));
-  if (hv) stx(hv + ko, ly.kt, PD, lm, W, Tq, M, D, A(1));
-  if (o_tan) sx2(o_tan + oo, ly.ot, PD, V, P, TV, lm, Tq, M, D, A(1));
+  // hV = Pdot^T W (W still in OP0), then V into OP0 for Odot = Pdot V + P tV
+  if (hv) stx(hv + ko, ly.kt, PD, lm, OP0, Tq, M, D, A(1));
+  __syncthreads();
+  load_mat(OP0, v + ko, M, D, ly.kt);
+  __syncthreads();
+  if (o_tan) sx2(o_tan + oo, ly.ot, PD, OP0, P, OP1, lm, Tq, M, D, A(1));
+  __syncthreads();
+  // P and Pdot are done: Q, tQ, K, tK again, into R0, for hQ and hK
+  if (hq || hk) {
+    load_qk(R0);
+    __syncthreads();
+    const A *Q = R0, *TQ = R0 + opq, *K = R0 + 2 * opq, *TK = K + opk;
+    if (hq) sx2(hq + qo, ly.qt, DSD, K, DS, TK, lm, Tq, M, D, A(s.scale));
+    if (hk) stx2(hk + ko, ly.kt, DSD, Q, DS, TQ, lm, Tq, M, D, A(s.scale));
+  }
 }
 
 #undef THERIA_ROWS

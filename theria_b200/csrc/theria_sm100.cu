@@ -178,6 +178,10 @@ bool f64_fits(const Shape& s, int n_q, int n_k, int n_s) {
   return small_eligible(s) &&
          small::smem_bytes((int)s.T, (int)s.M, (int)s.D, n_q, n_k, n_s, sizeof(double)) <= kMaxSmem;
 }
+bool f64_fits_hvp(const Shape& s) {
+  return small_eligible(s) &&
+         small::hvp_smem_bytes((int)s.T, (int)s.M, (int)s.D, sizeof(double)) <= kMaxSmem;
+}
 
 // The full-MAML head shape (T = M = 64, head dim 16, fp32) runs kernels
 // specialised at compile time; every other shape the generic ones.
@@ -267,7 +271,7 @@ int small_hvp(const void* q, const void* k, const void* v, const void* w, const 
               const void* tq, const void* tk, const void* tv, void* hq, void* hk, void* hv,
               void* o_tan, const Shape& s, cudaStream_t st, const small::Layout* lyp = nullptr) {
   const small::Layout ly = lyp ? *lyp : contiguous_layout(s);
-  const size_t sm = small::smem_bytes((int)s.T, (int)s.M, (int)s.D, 3, 4, 4, sizeof(A));
+  const size_t sm = small::hvp_smem_bytes((int)s.T, (int)s.M, (int)s.D, sizeof(A));
   auto kern = small::hvp_kernel<T, A>;
   if constexpr (std::is_same<T, float>::value && std::is_same<A, float>::value)
     if (small_spec<T, A>(s)) kern = small::hvp_kernel<T, A, 64, 16>;
@@ -695,7 +699,7 @@ int theria_sdpa_hvp(const void* q, const void* k, const void* v, const void* w,
   if (!workspace || workspace_bytes < simt_hvp_ws(s)) return THERIA_ERR_WORKSPACE;
   cudaStream_t st = (cudaStream_t)stream;
   if (dtype == THERIA_F64)
-    return f64_fits(s, 3, 4, 4) ? small_hvp<double, double>(q, k, v, w, lse, tq, tk, tv, hq, hk,
+    return f64_fits_hvp(s) ? small_hvp<double, double>(q, k, v, w, lse, tq, tk, tv, hq, hk,
                                                             hv, o_tan, s, st)
                                 : THERIA_ERR_UNSUPPORTED;
   if (small_eligible(s))
@@ -857,7 +861,7 @@ int theria_sdpa_qkv_hvp(const void* qkv, const void* w, const float* lse, const 
   Shape s{B, H, T, T, D, scale, causal ? 1 : 0};
   cudaStream_t st = (cudaStream_t)stream;
   if (dtype == THERIA_F64)
-    return f64_fits(s, 3, 4, 4)
+    return f64_fits_hvp(s)
                ? qkv_hvp<double, double>(qkv, w, lse, tqkv, hqkv, o_tan, s, st)
                : THERIA_ERR_UNSUPPORTED;
   return THERIA_DISPATCH(dtype, qkv_hvp, qkv, w, lse, tqkv, hqkv, o_tan, s, st);
