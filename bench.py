@@ -247,10 +247,9 @@ def cpu_fwdbwd_sample(budget_s=12.0, min_units=1, max_units=4096, dtype=torch.bf
 
 
 # ------------------------------------------------------------------ workloads
-def run_fwdbwd(args, world, rank, dev, causal=False, with_e2e=True):
+def run_fwdbwd(args, world, rank, dev, causal=False, with_e2e=True, dt=torch.bfloat16):
     from theria_b200.attention import ops
     B, H, N, D = CFG2["B"], CFG2["H"], CFG2["N"], CFG2["D"]
-    dt = torch.bfloat16
     gen = torch.Generator("cpu").manual_seed(rank)  # rank r owns shard r of the job
     q, k, v, do = (randn((B, H, N, D), gen, dt, dev) for _ in range(4))
 
@@ -383,6 +382,43 @@ def run_jvp_hvp(args, world, rank, dev):
             "hvp_ms": ms_h, "hvp_tflops": f("hvp", ms_h), "hvp_over_fwdbwd": ms_h / ms_fb}
 
 
+def run_strong_split(args, world, rank, dev, peak):
+    """The fixed configs split over the ranks (strong scaling): configs[1]'s
+    B*H = 64 (b, h) units and configs[2]'s 16 units are divided evenly, each
+    rank running its units as one [1, units, N, D] call; aggregate TFLOP/s =
+    the whole config's flops / the max rank time."""
+    from theria_b200.attention import ops
+    res = {}
+    for name, cfg, kinds in (("cfg2_fwdbwd", CFG2, ("fwdbwd",)),
+                             ("cfg3_jvp_hvp", CFG3, ("fwdbwd", "jvp", "hvp"))):
+        B, H, N, D = cfg["B"], cfg["H"], cfg["N"], cfg["D"]
+        units = B * H
+        per = units // world
+        gen = torch.Generator("cpu").manual_seed(100 + rank)
+        q, k, v, w, tq, tk, tv = (randn((1, per, N, D), gen, torch.bfloat16, dev)
+                                  for _ in range(7))
+        _, lse = ops.forward(q, k, v)
+        steps = max(5, args.steps)
+
+        def fb():
+            o, l2 = ops.forward(q, k, v)
+            ops.backward(q, k, v, w, l2, o=o)
+
+        fns = {"fwdbwd": fb, "jvp": lambda: ops.jvp(q, k, v, tq, tk, tv, lse),
+               "hvp": lambda: ops.hvp(q, k, v, w, lse, tq, tk, tv)}
+        out = {"units_total": units, "units_per_rank": per}
+        for kind in kinds:
+            ms, _ = timed(fns[kind], steps, 3, world)
+            tf = flops(kind, B, H, N, D) / (ms * 1e-3) / 1e12
+            out[kind + "_ms"] = ms
+            out[kind + "_tflops"] = tf
+            out[kind + "_frac"] = tf / peak
+        res[name] = out
+        del q, k, v, w, tq, tk, tv, lse
+    torch.cuda.empty_cache()
+    return res
+
+
 def run_maml(args, world, rank, dev, steps=None):
     """meta-batch 32 tasks sharded over the ranks, 5 inner SGD
     steps (lr 0.4, create_graph=True), Adam 1e-3, one gradient all-reduce."""
@@ -418,14 +454,18 @@ def run_maml(args, world, rank, dev, steps=None):
                     "so its launch counter sees them only at capture"}
 
 
-def run_sweep(args, world, rank, dev):
+def run_sweep(args, world, rank, dev, peak, points=None):
     """configs[4]: causal bf16, B=1, H=32, D in {64,128}, N in 512..16384;
-    heads sharded over the ranks (H/world each); fwd, fwd+bwd, JVP, HVP."""
+    heads sharded over the ranks (H/world each, strong split: the total is
+    fixed); fwd, fwd+bwd, JVP, HVP as aggregate TFLOP/s (all 32 heads' flops
+    over the max rank time) and as a fraction of the dense-bf16 peak."""
     from theria_b200.attention import ops
     H = 32 // world
     out = []
-    for D in (64, 128):
-        for N in (512, 1024, 2048, 4096, 8192, 16384):
+    if points is None:
+        points = [(D, N) for D in (64, 128) for N in (512, 1024, 2048, 4096, 8192, 16384)]
+    for D, N in points:
+        if True:
             gen = torch.Generator("cpu").manual_seed(rank)
             q, k, v, w, tq, tk, tv = (randn((1, H, N, D), gen, torch.bfloat16, dev)
                                       for _ in range(7))
@@ -439,14 +479,18 @@ def run_sweep(args, world, rank, dev):
             t_h, _ = timed(lambda: ops.hvp(q, k, v, w, lse, tq, tk, tv, causal=True), steps, 3,
                            world)
             f = lambda kind, ms: flops(kind, 1, 32, N, D, True) / (ms * 1e-3) / 1e12  # noqa: E731
-            out.append({"D": D, "N": N, "fwd_tflops": f("fwd", t_f),
-                        "fwdbwd_tflops": f("fwdbwd", t_f + t_b), "jvp_tflops": f("jvp", t_j),
-                        "hvp_tflops": f("hvp", t_h), "fwd_ms": t_f, "bwd_ms": t_b,
-                        "jvp_ms": t_j, "hvp_ms": t_h})
+            pt = {"D": D, "N": N, "fwd_tflops": f("fwd", t_f),
+                  "fwdbwd_tflops": f("fwdbwd", t_f + t_b), "jvp_tflops": f("jvp", t_j),
+                  "hvp_tflops": f("hvp", t_h), "fwd_ms": t_f, "bwd_ms": t_b,
+                  "jvp_ms": t_j, "hvp_ms": t_h}
+            for kind in ("fwd", "fwdbwd", "jvp", "hvp"):
+                pt[kind + "_frac"] = pt[kind + "_tflops"] / peak
+            out.append(pt)
             del q, k, v, w, tq, tk, tv, o, lse
     torch.cuda.empty_cache()
-    return {"config": "configs[4] causal bf16 B=1 H=32 (heads sharded), fwd+bwd = fwd + bwd "
-                      "launch times", "points": out}
+    return {"config": f"configs[4] causal bf16 B=1 H=32, {H} heads per rank (strong split), "
+                      "fwd+bwd = fwd + bwd launch times",
+            "peak_tflops": peak, "points": out}
 
 
 # ------------------------------------------------------------------ arms
@@ -492,27 +536,40 @@ def theria_arm(args, world, rank, local):
     all_cpus = os.sched_getaffinity(0)
     numa_cpus = bind_to_gpu_numa(dev)
     peaks, peak_src = load_peaks()
+    # every timed launch here is short (milliseconds, at most a few seconds of
+    # steps), so the burst dense-bf16 figure is the denominator
+    peak = peaks["bf16_tflops"]
     causal = args.workload == "fwdbwd_causal"
     res = run_fwdbwd(args, world, rank, dev, causal=causal)
+    _lib.check_device_error(local)
     extra = {}
     if not args.no_extra:
         extra["jvp_hvp"] = run_jvp_hvp(args, world, rank, dev)
         extra["maml"] = run_maml(args, world, rank, dev)
-        if args.sweep:
-            extra["long_seq_sweep"] = run_sweep(args, world, rank, dev)
         if not causal:
             c = run_fwdbwd(args, world, rank, dev, causal=True, with_e2e=False)
-            extra["fwdbwd_causal"] = {"tflops": c["value"], "ms_per_step": c["ms_per_step"]}
+            extra["fwdbwd_causal"] = {"tflops": c["value"], "ms_per_step": c["ms_per_step"],
+                                      "frac": c["value"] / world / peak}
+        f16 = run_fwdbwd(args, world, rank, dev, causal=causal, with_e2e=False,
+                         dt=torch.float16)
+        extra["fwdbwd_fp16"] = {"config": "configs[1] in fp16", "tflops": f16["value"],
+                                "ms_per_step": f16["ms_per_step"],
+                                "frac": f16["value"] / world / peak,
+                                "fwd_tflops": f16["fwd_tflops"], "bwd_tflops": f16["bwd_tflops"]}
+        extra["strong_split"] = run_strong_split(args, world, rank, dev, peak)
+        extra["long_seq_sweep"] = run_sweep(
+            args, world, rank, dev, peak,
+            points=None if args.sweep else [(64, 4096), (64, 16384), (128, 4096), (128, 16384)])
+        _lib.check_device_error(local)
     if rank != 0:
         return
-    peak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
     achieved = res["bwd_tflops"]
     key = "cfg2_causal" if causal else "cfg2"
     traffic = NCU_TRAFFIC_BYTES.get(key)
     roofline = {"kernel": "theria_sdpa_bwd (z prepass + dQ/dK/dV kernels of one call)",
                 "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                 "frac": achieved / peak, "traffic": traffic,
-                "peak_source": f"{peak_src} (bf16_tflops_sustained)",
+                "peak_source": f"{peak_src} (bf16_tflops, burst: each launch is timed alone)",
                 "algorithmic_flops_per_launch": flops("bwd", 4, 16, 4096, 128, causal),
                 "launch_ms": res["t_bwd_ms"],
                 "fwd": {"achieved": res["fwd_tflops"], "frac": res["fwd_tflops"] / peak,
@@ -611,7 +668,7 @@ def main():
     ap.add_argument("--workload", choices=["fwdbwd", "fwdbwd_causal"], default="fwdbwd")
     ap.add_argument("--no-extra", action="store_true")
     ap.add_argument("--sweep", action="store_true",
-                    help="add the configs[4] long-sequence causal sweep to `extra`")
+                    help="run every configs[4] sweep point (default: D 64/128 x N 4096/16384)")
     ap.add_argument("--cpu-budget", type=float, default=12.0,
                     help="seconds of CPU work for the cpu_baseline sample")
     ap.add_argument("--profile-case", choices=["fwdbwd", "jvp", "hvp", "maml_heads", "maml_step"],

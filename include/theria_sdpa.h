@@ -9,8 +9,11 @@
  *   lse                                    [B, H, T]  float32
  * D == Dv.  All input tensors of one call share `dtype`.  Nothing here
  * allocates device memory: outputs and the workspace are the caller's.
- * Calls are stream-ordered and asynchronous (no host synchronisation) and
- * keep no mutable global state.  Each returns a THERIA_* status.
+ * Calls are stream-ordered and asynchronous (no host synchronisation).
+ * The library's mutable state is limited to a per-device error word
+ * (theria_get_device_error), a process-wide launch counter, and the
+ * fixed scratch array of theria_sdpa_bwd_noalloc; no call keeps data
+ * between calls otherwise.  Each returns a THERIA_* status.
  *
  * Causal masking is top-left aligned: query row i attends to keys j <= i.
  *
@@ -138,12 +141,21 @@ int theria_sdpa_hvp(const void* q, const void* k, const void* v,
  * allocation of any kind.
  *
  * Limits: B*H*T*4 bytes must fit in THERIA_NOALLOC_SCRATCH_BYTES, else it
- * returns THERIA_ERR_SCRATCH_LIMIT without launching anything.  All calls
+ * returns THERIA_ERR_SCRATCH_LIMIT without launching anything.  Which
+ * kernels run depends on the size as well: the 16-bit tensor-core backward
+ * also keeps an fp32 dQ accumulator in the scratch, so it is used only when
+ * B*H*T*(D+1)*4 bytes (each part rounded up to 256) fit; larger accepted
+ * problems run the CUDA-core backward kernels -- same results within the
+ * usual tolerance, but far slower.  theria_sdpa_bwd_noalloc_uses_tc reports
+ * which path a shape takes.  All calls
  * on a GPU share the one array, so calls that overlap on the GPU (two
  * streams, or two host threads on different streams) race and corrupt each
  * other's results; serialise them.  The first call on each device looks up
- * the array's device address with that device current (one-time set-up);
- * make that first call before any stream capture.  The array keeps the last
+ * the array's device address with that device current (one-time set-up)
+ * and caches it for the life of the process; make that first call before
+ * any stream capture.  The cache does not survive cudaDeviceReset or the
+ * destruction of the device's primary context: do not call this entry
+ * point after either.  The array keeps the last
  * call's contents; nothing in it needs to start at zero (every element a
  * call reads was written earlier in that same call).
  */
@@ -153,6 +165,12 @@ int theria_sdpa_bwd_noalloc(const void* q, const void* k, const void* v,
                             const float* lse, void* dq, void* dk, void* dv,
                             int64_t B, int64_t H, int64_t T, int64_t M, int64_t D,
                             int dtype, float scale, int causal, void* stream);
+/* 1 if theria_sdpa_bwd_noalloc runs the tensor-core backward for this
+ * shape and dtype, 0 if it runs the CUDA-core kernels, or a negative
+ * THERIA_* status (negated) if it would refuse the problem.  Looks only at
+ * sizes (pointer alignment is assumed to be 16 bytes). */
+int theria_sdpa_bwd_noalloc_uses_tc(int64_t B, int64_t H, int64_t T, int64_t M, int64_t D,
+                                    int dtype);
 
 /*
  * Dense attention scores: out[b,h,t,m] = scale * sum_d q[b,h,t,d] k[b,h,m,d],
@@ -208,6 +226,19 @@ int64_t theria_launch_count(void);
  */
 int theria_get_device_error(int* out_flag, void* stream);
 int theria_clear_device_error(void* stream);
+
+/*
+ * Diagnostic of the bounded device-side waits (no counterpart in the
+ * reference).  Launches one CTA whose first warp waits, with a limit of
+ * `max_polls` polls (1 .. 2^20), on an mbarrier phase that nothing
+ * completes, and whose second warp waits on the same phase with the
+ * library's normal limit.  The first warp must give up, set the device
+ * error word to THERIA_ERR_DEVICE_TIMEOUT and raise the CTA's abort flag;
+ * the second must then unwind.  `out` is 2 device ints: out[0] = 1 if the
+ * first wait gave up, out[1] = 1 if the second unwound.  No wait in it is
+ * unbounded, and the kernel leaves the GPU context usable.
+ */
+int theria_diag_bounded_wait(int max_polls, int* out, void* stream);
 
 #ifdef __cplusplus
 }

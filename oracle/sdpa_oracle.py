@@ -33,6 +33,8 @@ __all__ = [
     "hvp_sum",
     "hvp_autograd",
     "hvp_fd",
+    "attention_rows",
+    "jvp_rows",
 ]
 
 
@@ -206,3 +208,41 @@ def hvp_fd(grad_fn, q, k, v, tq, tk, tv, eps=1e-3):
     gp = grad_fn(q + eps * tq, k + eps * tk, v + eps * tv)
     gm = grad_fn(q - eps * tq, k - eps * tk, v - eps * tv)
     return tuple((a - b) * (0.5 / eps) for a, b in zip(gp, gm))
+
+
+def _row_mask(rows, M):
+    # causal mask for query rows at absolute positions `rows` (top-left aligned)
+    return torch.arange(M).unsqueeze(0) > rows.unsqueeze(1)
+
+
+def attention_rows(q, k, v, rows, scale=None, causal=False):
+    """Rows ``rows`` of O and of the row LSE, computed in fp64 from only those
+    query rows: row i of ``reference_attention.py:9-19`` depends on q_i and
+    all of K, V, so long sequences are checked on a sample of rows.
+
+    q, k, v are one head each ([N, D] or [M, D]); returns (O[rows], LSE[rows]).
+    """
+    scale = _scale(q, scale)
+    qr = q[rows].double()
+    s = torch.matmul(qr, k.double().transpose(-2, -1)) * scale
+    if causal:
+        s = s.masked_fill(_row_mask(rows, k.shape[0]), float("-inf"))
+    lse = torch.logsumexp(s, dim=-1)
+    return torch.matmul(torch.exp(s - lse.unsqueeze(-1)), v.double()), lse
+
+
+def jvp_rows(q, k, v, tq, tk, tv, rows, scale=None, causal=False):
+    """Rows ``rows`` of the exact tangent Odot (fp64), as ``jvp`` computes it
+    (``reference_jvp_sdpa.py:21-44``) but from only those query rows."""
+    scale = _scale(q, scale)
+    qr, tqr = q[rows].double(), tq[rows].double()
+    kf, vf, tkf, tvf = k.double(), v.double(), tk.double(), tv.double()
+    s = torch.matmul(qr, kf.transpose(-2, -1)) * scale
+    sd = (torch.matmul(tqr, kf.transpose(-2, -1)) + torch.matmul(qr, tkf.transpose(-2, -1))) * scale
+    if causal:
+        mask = _row_mask(rows, k.shape[0])
+        s = s.masked_fill(mask, float("-inf"))
+        sd = sd.masked_fill(mask, 0.0)
+    p = torch.softmax(s, dim=-1)
+    pd = p * (sd - (sd * p).sum(dim=-1, keepdim=True))
+    return torch.matmul(pd, vf) + torch.matmul(p, tvf)

@@ -131,3 +131,20 @@ def test_maml_helper_arguments_checked_on_the_host():
     assert lib.theria_gelu_bwd2(None, None, None, None, None, 0, None) == _lib.THERIA_OK
     assert lib.theria_ln_bwd2(p, p, 64, p, p, p, 8, p, 64, p, p, p, p, 1 << 20, 4, 100, 64,
                               1e-5, None) == _lib.THERIA_ERR_INVALID_ARG  # lda < D
+
+
+def test_diag_wait_and_noalloc_query_checked_on_the_host():
+    lib = _lib.load()
+    p = ctypes.c_void_p(16)
+    assert lib.theria_diag_bounded_wait(0, p, None) == _lib.THERIA_ERR_INVALID_ARG
+    assert lib.theria_diag_bounded_wait(1 << 21, p, None) == _lib.THERIA_ERR_INVALID_ARG
+    assert lib.theria_diag_bounded_wait(5, None, None) == _lib.THERIA_ERR_INVALID_ARG
+    # which backward the allocation-free entry point runs, from sizes alone
+    assert lib.theria_sdpa_bwd_noalloc_uses_tc(1, 2, 257, 257, 128, _lib.BF16) == 1
+    assert lib.theria_sdpa_bwd_noalloc_uses_tc(1, 4, 2048, 2048, 128, _lib.BF16) == 0
+    assert lib.theria_sdpa_bwd_noalloc_uses_tc(1, 2, 200, 200, 64, _lib.F32) == 0
+    assert lib.theria_sdpa_bwd_noalloc_uses_tc(4, 16, 4096, 4096, 128, _lib.BF16) == 0
+    assert lib.theria_sdpa_bwd_noalloc_uses_tc(1, 16, 131072, 131072, 64, _lib.BF16) == \
+        -_lib.THERIA_ERR_SCRATCH_LIMIT
+    assert lib.theria_sdpa_bwd_noalloc_uses_tc(1, 1, 8, 8, 0, _lib.BF16) == \
+        -_lib.THERIA_ERR_INVALID_ARG

@@ -19,6 +19,7 @@ import ctypes
 import pytest
 import torch
 
+from oracle import sdpa_oracle as orc
 from tests._util import max_abs, max_rel
 
 pytestmark = pytest.mark.gpu
@@ -62,14 +63,26 @@ def _bwd_noalloc(lib, q, k, v, o, do, lse, causal):
     return outs
 
 
-@pytest.mark.parametrize("dtype,shape,causal", [
-    (torch.float32, (2, 2, 64, 32), False),
-    (torch.float32, (1, 4, 64, 16), True),
-    (torch.bfloat16, (1, 2, 257, 128), False),
-    (torch.float16, (2, 2, 130, 64), True),
-])
-def test_noalloc_matches_regular_backward_twice(dtype, shape, causal):
+# (dtype, shape, causal, path the noalloc entry point should take): 1 = the
+# tensor-core backward, 0 = whole-head or CUDA-core kernels.  fp32 T > 64
+# and the bf16 (1, 4, 2048, 128) case keep their row terms in the scratch
+# array; the latter's fp32 dQ accumulator does not fit beside them, so it
+# runs the CUDA-core kernels.
+CASES = [
+    (torch.float32, (2, 2, 64, 32), False, 0),
+    (torch.float32, (1, 4, 64, 16), True, 0),
+    (torch.float32, (1, 2, 200, 64), True, 0),
+    (torch.bfloat16, (1, 2, 257, 128), False, 1),
+    (torch.float16, (2, 2, 130, 64), True, 1),
+    (torch.bfloat16, (1, 4, 2048, 128), False, 0),
+]
+
+
+@pytest.mark.parametrize("dtype,shape,causal,tc", CASES)
+def test_noalloc_matches_regular_backward_twice(dtype, shape, causal, tc):
     lib = _lib.load()
+    B, H, T, D = shape
+    assert lib.theria_sdpa_bwd_noalloc_uses_tc(B, H, T, T, D, CODE[dtype]) == tc
     for call, seed in enumerate((11, 12)):  # two calls in a row, different data
         q, k, v, do = _inputs(shape, dtype, seed)
         o, lse = ops.forward(q, k, v, causal=causal)
@@ -81,6 +94,17 @@ def test_noalloc_matches_regular_backward_twice(dtype, shape, causal):
                 assert max_rel(a, b) <= 1e-5, (call, name)
             else:
                 assert max_abs(a, b) <= 2e-2, (call, name)
+        if call == 0:
+            # the first call also against the CPU oracle (two heads at most)
+            hs = slice(0, 2)
+            qc, kc, vc, dc = (t[:1, hs].float().cpu() for t in (q, k, v, do))
+            ref = orc.backward(qc, kc, vc, dc, causal=causal)
+            for a, b, name in zip(got, ref, ("dq", "dk", "dv")):
+                a = a[:1, hs].float().cpu()
+                if dtype == torch.float32:
+                    assert max_rel(a, b) <= 1e-5, ("oracle", name)
+                else:
+                    assert max_abs(a, b) <= 2e-2, ("oracle", name)
 
 
 def test_noalloc_refuses_problems_beyond_its_scratch():
@@ -91,3 +115,5 @@ def test_noalloc_refuses_problems_beyond_its_scratch():
                                      1, 16, 131072, 128, 64, _lib.BF16, 0.125, 0, None)
     assert st == _lib.THERIA_ERR_SCRATCH_LIMIT
     assert b"scratch" in lib.theria_status_string(st)
+    assert lib.theria_sdpa_bwd_noalloc_uses_tc(1, 16, 131072, 131072, 64, _lib.BF16) == \
+        -_lib.THERIA_ERR_SCRATCH_LIMIT

@@ -7,6 +7,7 @@ contracts (with create_graph=True double-backward) and the
 a C ABI (include/theria_sdpa.h, libtheria_sm100.so).
 """
 
+from theria_b200._lib import check_device_error  # noqa: F401
 from theria_b200.autograd.sdpa_function import sdpa  # noqa: F401
 
 __version__ = "0.1.0"

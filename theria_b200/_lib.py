@@ -46,6 +46,7 @@ SIGNATURES = {
     "theria_sdpa_jvp": (_i, [_vp] * 8 + [_i64] * 5 + [_i, _f, _i, _vp]),
     "theria_sdpa_hvp": (_i, [_vp] * 12 + [_vp, _i64] + [_i64] * 5 + [_i, _f, _i, _vp]),
     "theria_sdpa_bwd_noalloc": (_i, [_vp] * 10 + [_i64] * 5 + [_i, _f, _i, _vp]),
+    "theria_sdpa_bwd_noalloc_uses_tc": (_i, [_i64] * 5 + [_i]),
     "theria_sdpa_scores": (_i, [_vp, _vp, _vp, _i] + [_i64] * 5 + [_i, _f, _vp]),
     "theria_sdpa_probs": (_i, [_vp] * 4 + [_i64] * 5 + [_i, _f, _i, _vp]),
     "theria_sdpa_qkv_fwd": (_i, [_vp] * 3 + [_i64] * 4 + [_i, _f, _i, _vp]),
@@ -65,6 +66,7 @@ SIGNATURES = {
                             _vp, _i64, _i64, _i64, _i64, _f, _vp]),
     "theria_get_device_error": (_i, [ctypes.POINTER(ctypes.c_int), _vp]),
     "theria_clear_device_error": (_i, [_vp]),
+    "theria_diag_bounded_wait": (_i, [_i, _vp, _vp]),
 }
 
 _lib = None
@@ -107,3 +109,32 @@ def ptr(t):
 
 def stream_of(t: torch.Tensor):
     return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def device_error(device=None) -> int:
+    """The device-side error word of `device` (synchronises its current stream)."""
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
+    flag = ctypes.c_int(0)
+    with torch.cuda.device(dev):
+        st = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+        check(load().theria_get_device_error(ctypes.byref(flag), st), "theria_get_device_error")
+    return flag.value
+
+
+def clear_device_error(device=None) -> None:
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
+    with torch.cuda.device(dev):
+        st = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+        check(load().theria_clear_device_error(st), "theria_clear_device_error")
+
+
+def check_device_error(device=None, clear: bool = True) -> None:
+    """Raise TheriaError if a kernel's bounded device-side wait gave up on
+    `device` since the word was last cleared (its outputs are then partly
+    written).  Clears the word before raising when `clear` is set."""
+    flag = device_error(device)
+    if flag != THERIA_OK:
+        if clear:
+            clear_device_error(device)
+        msg = load().theria_status_string(flag).decode()
+        raise TheriaError(f"device-side error: {msg} (status {flag})")

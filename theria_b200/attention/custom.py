@@ -3,7 +3,10 @@
 Mirrors ``theria/attention/custom.py:15-71``.  The ``backend=`` switch keeps
 the reference's names:
 
-* ``triton_full_fused`` (default here), ``triton_full_fused_phase8``,
+* ``triton_full_fused`` (default here; the reference defaults to
+  ``reference``, and ``theria.attention.custom.sdpa_custom`` installed by
+  ``theria_b200.compat.install_as_theria`` keeps that default),
+  ``triton_full_fused_phase8``,
   ``fused``: the fused sm_100a operator (twice differentiable, forward-mode
   capable);
 * ``custom``: ``SDPACustom`` (the same kernels behind the reference's
@@ -24,18 +27,13 @@ from __future__ import annotations
 import torch
 
 from theria_b200.attention.fused import SDPAFunction
+from theria_b200.attention.reference import reference_attention
 from theria_b200.attention.triton_qk import triton_qk, triton_qk_fast, triton_qk_softmax
 from theria_b200.autograd.sdpa_custom_function import SDPACustom
 
 FUSED_BACKENDS = ("triton_full_fused", "triton_full_fused_phase8", "custom", "fused")
 PARTIAL_BACKENDS = ("triton_qk", "triton_ref", "triton", "triton_fast", "triton_qk_softmax")
 BACKENDS = FUSED_BACKENDS + PARTIAL_BACKENDS + ("reference",)
-
-
-def _reference_formula(q, k, v):
-    # reference_attention.py:9-19: softmax(q k^T / sqrt(D)) v
-    scores = torch.matmul(q, k.transpose(-2, -1)) / (q.shape[-1] ** 0.5)
-    return torch.matmul(torch.softmax(scores, dim=-1), v)
 
 
 def sdpa_custom(q, k, v, *, backend: str = "triton_full_fused", causal: bool = False):
@@ -54,7 +52,7 @@ def sdpa_custom(q, k, v, *, backend: str = "triton_full_fused", causal: bool = F
     if backend in FUSED_BACKENDS:
         return SDPAFunction.apply(q, k, v, causal, None)
     if backend == "reference":
-        return _reference_formula(q, k, v)
+        return reference_attention(q, k, v)
     if backend == "triton_qk_softmax":
         probs = triton_qk_softmax(q, k).to(torch.float32)
         return torch.matmul(probs, v.to(probs.dtype)).to(q.dtype)

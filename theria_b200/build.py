@@ -45,7 +45,8 @@ def up_to_date():
     if not os.path.exists(LIB):
         return False
     t = os.path.getmtime(LIB)
-    deps = sources() + [os.path.join(ROOT, "include", "theria_sdpa.h"), __file__]
+    deps = sources() + [os.path.join(ROOT, "include", h) for h in ("theria_sdpa.h", "theria_ln.h")]
+    deps.append(__file__)
     return all(os.path.getmtime(p) <= t for p in deps if os.path.exists(p))
 
 

@@ -66,8 +66,9 @@ constexpr uint32_t kMaxPolls = 1u << 22;
 // sets the device error word) if it does not within kMaxPolls polls, or if
 // another thread of the CTA already gave up (*abort != 0).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
-                                          volatile int* abort) {
-  for (uint32_t i = 0; i < kMaxPolls; ++i) {
+                                          volatile int* abort,
+                                          uint32_t max_polls = kMaxPolls) {
+  for (uint32_t i = 0; i < max_polls; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 1023) == 1023 && *abort) return false;
   }

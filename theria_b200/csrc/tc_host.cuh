@@ -70,11 +70,15 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 // The tensor-core kernels take 16-bit inputs with head dim 64 or 128 and
 // sizes that fit TMA's 32-bit coordinates.
-inline bool tc_eligible(int dtype, int64_t T, int64_t M, int64_t D, int64_t BH) {
+// Dtype and size conditions of the tensor-core kernels alone.
+inline bool tc_shape_ok(int dtype, int64_t T, int64_t M, int64_t D, int64_t BH) {
   if (dtype != THERIA_BF16 && dtype != THERIA_F16) return false;
   if (D != 64 && D != 128) return false;
-  if (T >= (1ll << 31) || M >= (1ll << 31) || BH >= 65536) return false;
-  return encode_fn() != nullptr;
+  return T < (1ll << 31) && M < (1ll << 31) && BH < 65536;
+}
+
+inline bool tc_eligible(int dtype, int64_t T, int64_t M, int64_t D, int64_t BH) {
+  return tc_shape_ok(dtype, T, M, D, BH) && encode_fn() != nullptr;
 }
 
 }  // namespace tc

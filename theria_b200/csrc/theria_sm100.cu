@@ -718,6 +718,46 @@ int theria_sdpa_hvp(const void* q, const void* k, const void* v, const void* w,
                          (float*)workspace, s, st);
 }
 
+}  // extern "C"
+
+namespace theria {
+namespace {
+// Diagnostic of the bounded-wait machinery every tensor-core kernel uses:
+// warp 0 waits on an mbarrier phase that nothing completes, with a poll
+// limit of `max_polls`, and must give up (setting the abort flag and the
+// device error word); warp 1 waits on the same phase with the kernels'
+// normal limit and must unwind when it sees the abort flag.  out[0] = 1 if
+// warp 0 gave up, out[1] = 1 if warp 1 unwound.  The barrier's phase is
+// then completed by an arrival so the CTA exits with nothing pending.
+__global__ void __launch_bounds__(64) diag_bounded_wait_kernel(uint32_t max_polls, int* out) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ volatile int abort_flag;
+  if (threadIdx.x == 0) {
+    tc::mbar_init(&bar, 1);
+    abort_flag = 0;
+    tc::fence_barrier_init();
+  }
+  __syncthreads();
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (lane == 0) {
+    const bool ok = warp == 0 ? tc::mbar_wait(&bar, 0, &abort_flag, max_polls)
+                              : tc::mbar_wait(&bar, 0, &abort_flag);
+    out[warp] = ok ? 0 : 1;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) tc::mbar_arrive(&bar);
+}
+}  // namespace
+}  // namespace theria
+
+extern "C" {
+
+int theria_diag_bounded_wait(int max_polls, int* out, void* stream) {
+  if (max_polls < 1 || max_polls > (1 << 20) || out == nullptr) return THERIA_ERR_INVALID_ARG;
+  theria::diag_bounded_wait_kernel<<<1, 64, 0, (cudaStream_t)stream>>>((uint32_t)max_polls, out);
+  return theria::launch_status();
+}
+
 int theria_get_device_error(int* out_flag, void* stream) {
   if (!out_flag) return THERIA_ERR_INVALID_ARG;
   cudaStream_t st = (cudaStream_t)stream;
@@ -773,6 +813,16 @@ int theria_sdpa_bwd_noalloc(const void* q, const void* k, const void* v, const v
   return theria_sdpa_bwd(q, k, v, o, o_dtype, dout, lse, dq, dk, dv, scratch,
                          (int64_t)THERIA_NOALLOC_SCRATCH_BYTES, B, H, T, M, D, dtype, scale,
                          causal, stream);
+}
+
+int theria_sdpa_bwd_noalloc_uses_tc(int64_t B, int64_t H, int64_t T, int64_t M, int64_t D,
+                                    int dtype) {
+  if (int e = check_shape(B, H, T, M, D, dtype)) return -e;
+  if (B * H * T * 4 > (int64_t)THERIA_NOALLOC_SCRATCH_BYTES) return -THERIA_ERR_SCRATCH_LIMIT;
+  Shape s{B, H, T, M, D, 1.f, 0};
+  if (dtype == THERIA_F64 || small_eligible(s)) return 0;
+  return tc::tc_shape_ok(dtype, T, M, D, B * H) &&
+         tc_bwd_ws(s) <= (int64_t)THERIA_NOALLOC_SCRATCH_BYTES;
 }
 
 }  // extern "C"

@@ -99,6 +99,12 @@ class GraphedMetaStep:
     (``MetaStep(..., capturable=True)``); the task batch shapes are fixed
     at capture.  Under torch.distributed the all-reduce is captured too
     (NCCL supports capture; the communicator is warmed up first).
+
+    Construction is not free of side effects: the ``warmup`` eager
+    meta-steps run before capture are real steps on ``example``, so they
+    update the model's parameters and the optimizer's state (Adam moments
+    and step count) ``warmup`` times.  Save and restore both around the
+    constructor if the model must start from its current state.
     """
 
     def __init__(self, meta_step: "MetaStep", example: TaskBatch, warmup: int = 3):

@@ -33,12 +33,16 @@ def _rows(x, w):
 def _ldw(w):
     if w.stride(1) != 1:
         raise ValueError("layer_norm: affine rows must be contiguous")
-    return w.stride(0)
+    return w.shape[1] if w.shape[0] == 1 else w.stride(0)  # one row: its stride is unused
 
 
 def _rowwise(t):
     # [nt, D] with unit column stride (rows may be strided views of a flat
     # per-task buffer); anything else is packed
+    if t.shape[0] == 1 and t.stride(1) == 1:
+        # one row: only row 0 is read, so its row stride is irrelevant; give
+        # the kernels a view whose stride satisfies their ld >= D check
+        return t.as_strided(t.shape, (t.shape[1], 1))
     return t if t.stride(1) == 1 and (t.stride(0) >= t.shape[1] or t.stride(0) == 0) \
         else t.contiguous()
 
