@@ -15,7 +15,7 @@
 // TMEM: S^T [0,64), Sd^T [64,128), dP^T [128,192), dPd^T [192,256),
 // hV [256, 256+D), hK [256+D, 256+2D), pair hQ [384, 448) for D = 64.
 // Warp roles: 0 TMA, 1 issues the S-group products (and owns TMEM), 2
-// issues hK, hV and hQ, 3..10 compute, 11..14 hQ flush.  With the two groups
+// issues hK, hV and hQ, 3 idle, 4..11 compute, 12..15 hQ flush.  With the two groups
 // on separate threads the next tile's S-group (D = 64) runs on the tensor
 // core while the CUDA cores still work on the current tile; for D = 128 the
 // S-group waits for hQ^T to leave the S^T columns.
@@ -28,8 +28,15 @@ namespace tchvp {
 
 constexpr int BK = 128, BQ = 64;
 constexpr int NCOMPUTE = 256, NDQ = 128;
-constexpr int NTHREADS = 96 + NCOMPUTE + NDQ;
-constexpr int kFirstCompute = 3;
+// Four warpgroups: control (TMA, two MMA issuers, one idle warp), two of
+// compute, one of hQ flush.  Registers are moved from the control and flush
+// groups to the compute groups (setmaxnreg), whose threads hold four
+// 32-column rows of scores at once.
+constexpr int NTHREADS = 128 + NCOMPUTE + NDQ;
+constexpr int kFirstCompute = 4;
+constexpr int kRegCtl = 112, kRegCompute = 144, kRegFlush = 112;
+static_assert((kRegCtl + 2 * kRegCompute + kRegFlush) * 128 <= 65536,
+              "register split exceeds the launch allocation");
 
 template <int HD>
 struct Cfg {
@@ -113,6 +120,8 @@ hvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
   const uint32_t tmem = *tmem_slot;
   const uint32_t t_hv = tmem + 256, t_hk = tmem + 256 + HD, t_hqp = tmem + 384;
 
+  if (warp < kFirstCompute)
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegCtl));
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0 && n_iter > 0) {
@@ -246,8 +255,11 @@ hvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
         tc::mbar_wait_drain(drain + 1, 0);
       }
     }
+  } else if (warp < kFirstCompute) {
+    // warp 3: no role (it completes the control warpgroup)
   } else if (warp < kFirstCompute + NCOMPUTE / 32) {
     // ------------------------------------------------------------ compute
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegCompute));
     const int grp = (warp - kFirstCompute) >> 2;
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;  // TMEM lane = key row
@@ -355,6 +367,7 @@ hvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
     }
   } else {
     // ------------------------------------------------------------ hQ flush
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegFlush));
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
