@@ -35,7 +35,10 @@ constexpr int NCOMPUTE = 256, NDQ = 128;
 constexpr int NTHREADS = 128 + NCOMPUTE + NDQ;
 constexpr int kFirstCompute = 4;
 constexpr int kRegCtl = 112, kRegCompute = 144, kRegFlush = 112;
-static_assert((kRegCtl + 2 * kRegCompute + kRegFlush) * 128 <= 65536,
+// a warp's launch allocation is the largest multiple of 8 registers that
+// fits NTHREADS threads in 64K; a split above it would wait forever
+static_assert((kRegCtl + 2 * kRegCompute + kRegFlush) * 128 <=
+                  (65536 / NTHREADS) / 8 * 8 * NTHREADS,
               "register split exceeds the launch allocation");
 
 template <int HD>

@@ -282,6 +282,16 @@ int small_hvp(const void* q, const void* k, const void* v, const void* w, const 
   return launch_status();
 }
 
+// Kernels that move registers between warpgroups (setmaxnreg) need the
+// launch allocation their split assumes, or the raising warps would wait
+// forever; checked once per kernel before its first launch.
+template <typename K>
+bool regs_cover_split(K kern, int nthreads, int split_sum_per_128) {
+  cudaFuncAttributes a{};
+  if (cudaFuncGetAttributes(&a, kern) != cudaSuccess) return false;
+  return (int64_t)a.numRegs * nthreads >= (int64_t)split_sum_per_128 * 128;
+}
+
 // ------------------------------------------------------ tensor-core launches
 template <typename T, int HD, bool CAUSAL>
 int tc_fwd_launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, void* o,
@@ -436,6 +446,9 @@ int tc_hvp_launch(const CUtensorMap* m, const float* lse, const float* stats, fl
                   void* hk, void* hv, const Shape& s, cudaStream_t st) {
   using C = tchvp::Cfg<HD>;
   auto kern = tchvp::hvp_kernel<T, HD, CAUSAL>;
+  static const bool regs_ok = regs_cover_split(
+      kern, tchvp::NTHREADS, tchvp::kRegCtl + 2 * tchvp::kRegCompute + tchvp::kRegFlush);
+  if (!regs_ok) return THERIA_ERR_LAUNCH;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kAlloc);
   dim3 grid((unsigned)((s.M + tchvp::BK - 1) / tchvp::BK), (unsigned)(s.B * s.H));
   if (CAUSAL) grid = dim3(grid.y, grid.x);  // head index in x: longest tiles first
