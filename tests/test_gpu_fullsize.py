@@ -159,3 +159,23 @@ def test_cfg2_fp16_fwd_bwd_slices_match_oracle(causal):
         assert max_abs(_slice(o, b, h), orc.attention(qs, ks, vs, causal=causal)) <= TOL
         for x, r in zip((dq, dk, dv), orc.backward(qs, ks, vs, ds, causal=causal)):
             assert max_abs(_slice(x, b, h), r) <= TOL
+
+
+# ---------------------------------------------------------------- HVP query split
+# At small B*H the HVP's second pass splits each key tile's queries over up
+# to four CTAs and adds their hK/hV partial sums in fp32; these shapes take
+# that path (two chunks of unequal length, a ragged last query tile, T != M).
+@pytest.mark.parametrize("shape", [(1, 2, 2000, 2000, 64), (1, 2, 2100, 2000, 128),
+                                   (1, 1, 2048, 2048, 64)])
+def test_hvp_query_split_matches_oracle(shape):
+    B, H, T, M, D = shape
+    g = torch.Generator("cpu").manual_seed(7)
+    q, w, tq = (torch.randn(B, H, T, D, generator=g).to(torch.bfloat16) for _ in range(3))
+    k, v, tk, tv = (torch.randn(B, H, M, D, generator=g).to(torch.bfloat16) for _ in range(4))
+    dev = [t.cuda() for t in (q, k, v, w, tq, tk, tv)]
+    _, lse = ops.forward(*dev[:3])
+    hs = ops.hvp(dev[0], dev[1], dev[2], dev[3], lse, dev[4], dev[5], dev[6])
+    torch.cuda.synchronize()
+    ref = orc.hvp(*(t.float() for t in (q, k, v, w, tq, tk, tv)))
+    for x, r in zip(hs, ref):
+        assert max_abs(x.float().cpu(), r) <= TOL

@@ -75,7 +75,7 @@ hvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
            const float* __restrict__ lse,
            const float* __restrict__ stats, int64_t n_rows_total, float* __restrict__ hq_acc,
            T* __restrict__ hk, T* __restrict__ hv, int Tq, int M, float scale,
-           float scale_log2) {
+           float scale_log2, float* __restrict__ hkv_acc, int n_split) {
   using C = Cfg<HD>;
   constexpr bool kPair = (HD == 64);
   constexpr int ST = C::ST;
@@ -95,8 +95,15 @@ hvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
   const int bh = CAUSAL ? blockIdx.x : blockIdx.y;
   const int k0 = (CAUSAL ? blockIdx.y : blockIdx.x) * BK;
   const int n_qt = (Tq + BQ - 1) / BQ;
-  const int i_begin = CAUSAL ? k0 / BQ : 0;
-  const int n_iter = n_qt > i_begin ? n_qt - i_begin : 0;
+  // With n_split > 1 the query tiles that see this key tile are divided into
+  // n_split chunks (gridDim.z), each an even number of tiles so that dQ-style
+  // pairs never straddle two CTAs; hK and hV are then partial sums, added in
+  // fp32 into hkv_acc [2][B*H][M][D] (hV, then hK already scaled).
+  const int i_first = CAUSAL ? k0 / BQ : 0;
+  const int n_all = n_qt > i_first ? n_qt - i_first : 0;
+  const int chunk = n_split > 1 ? (((n_all + n_split - 1) / n_split + 1) & ~1) : n_all;
+  const int i_begin = i_first + (int)blockIdx.z * chunk;
+  const int n_iter = n_qt - i_begin < chunk ? (n_qt > i_begin ? n_qt - i_begin : 0) : chunk;
 
   if (threadIdx.x == 0) {
     tc::mbar_init(kv_full, 1);
@@ -337,7 +344,32 @@ hvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       ok = wait(mma2_done + (tl & 1), (tl >> 1) & 1);
       if (ok) tc::tc_fence_after();
     }
-    if (ok) {
+    if (ok && n_split > 1) {
+      // partial sums of this chunk of queries, added in fp32 (the TMEM loads
+      // are warp-collective: every lane loads, lanes past M skip the add)
+      if (n_iter > 0) {
+        const bool store = key < M;
+        const size_t base = ((size_t)bh * M + (store ? key : 0)) * HD;
+        const size_t plane = (size_t)(CAUSAL ? gridDim.x : gridDim.y) * M * HD;  // B*H*M*D
+#pragma unroll 1
+        for (int which = 0; which < 2; ++which) {
+          if ((which == 0 ? (void*)hv : (void*)hk) == nullptr) continue;
+          const float mul = which == 0 ? 1.f : scale;
+          const uint32_t col = which == 0 ? t_hv : t_hk;
+          float* acc = hkv_acc + which * plane + base;
+#pragma unroll 1
+          for (int c = grp * (HD / 64); c < (grp + 1) * (HD / 64); ++c) {
+            float v[32];
+            tc::tmem_ld32(col + lane_off + c * 32, v);
+            if (!store) continue;
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              tcbwd::red_add_v4(acc + c * 32 + 4 * i, v[4 * i] * mul, v[4 * i + 1] * mul,
+                                v[4 * i + 2] * mul, v[4 * i + 3] * mul);
+          }
+        }
+      }
+    } else if (ok) {
       const bool store = key < M;
       const size_t base = ((size_t)bh * M + (store ? key : 0)) * HD;
 #pragma unroll 1

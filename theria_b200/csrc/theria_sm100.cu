@@ -437,26 +437,62 @@ int tc_jvp(const void* q, const void* k, const void* v, const void* tq, const vo
 }
 
 int64_t simt_hvp_ws(const Shape& s) { return align_up(3 * s.B * s.H * s.T * 4); }
-int64_t tc_hvp_ws(const Shape& s) {
-  return align_up(3 * s.B * s.H * s.T * 4) + align_up(s.B * s.H * s.T * s.D * 4);
+// Query-chunk count of the HVP's second pass: the (key tile, b*h) units are
+// few against the SMs at small B*H (configs[2]: 256 CTAs = 1.7 waves on 148
+// SMs), so the queries of each key tile may be split over up to 4 CTAs
+// whose hK/hV partial sums are added in fp32; chosen for the fullest last
+// wave, preferring fewer chunks unless that wave fills >= 5 % better.  Each
+// chunk keeps at least 16 query tiles: with 8 (configs[2] in 4 chunks) the
+// per-CTA start-up cost outweighed the fuller wave (505 -> 447 TFLOP/s).
+int hvp_split(const Shape& s, int sms) {
+  const int64_t units = s.B * s.H * ((s.M + tchvp::BK - 1) / tchvp::BK);
+  const int64_t n_qt = (s.T + tchvp::BQ - 1) / tchvp::BQ;
+  if (s.causal || units >= 8 * (int64_t)sms) return 1;
+  int best = 1;
+  double best_eff = 0.0;
+  for (int k = 1; k <= 4; ++k) {
+    if (k > 1 && n_qt / k < 16) break;
+    const int64_t ctas = units * k;
+    const double eff = (double)ctas / (double)(((ctas + sms - 1) / sms) * sms);
+    if (eff > best_eff + 0.05) {
+      best = k;
+      best_eff = eff;
+    }
+  }
+  return best;
+}
+
+int64_t tc_hvp_ws(const Shape& s, int split) {
+  return align_up(3 * s.B * s.H * s.T * 4) + align_up(s.B * s.H * s.T * s.D * 4) +
+         (split > 1 ? align_up(2 * s.B * s.H * s.M * s.D * 4) : 0);
+}
+int64_t tc_hvp_ws(const Shape& s) { return tc_hvp_ws(s, hvp_split(s, 148)); }
+
+int sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+    return 148;
+  return n;
 }
 
 template <typename T, int HD, bool CAUSAL>
 int tc_hvp_launch(const CUtensorMap* m, const float* lse, const float* stats, float* hq_acc,
-                  void* hk, void* hv, const Shape& s, cudaStream_t st) {
+                  void* hk, void* hv, float* hkv_acc, int split, const Shape& s,
+                  cudaStream_t st) {
   using C = tchvp::Cfg<HD>;
   auto kern = tchvp::hvp_kernel<T, HD, CAUSAL>;
   static const bool regs_ok = regs_cover_split(
       kern, tchvp::NTHREADS, tchvp::kRegCtl + 2 * tchvp::kRegCompute + tchvp::kRegFlush);
   if (!regs_ok) return THERIA_ERR_LAUNCH;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kAlloc);
-  dim3 grid((unsigned)((s.M + tchvp::BK - 1) / tchvp::BK), (unsigned)(s.B * s.H));
-  if (CAUSAL) grid = dim3(grid.y, grid.x);  // head index in x: longest tiles first
+  dim3 grid((unsigned)((s.M + tchvp::BK - 1) / tchvp::BK), (unsigned)(s.B * s.H), split);
+  if (CAUSAL) grid = dim3(grid.y, grid.x, split);  // head index in x: longest tiles first
   kern<<<grid, tchvp::NTHREADS, C::kAlloc, st>>>(m[0], m[1], m[2], m[3], m[4], m[5], m[6], m[7],
                                                  lse,
                                                  stats, s.B * s.H * s.T, hq_acc, (T*)hk,
                                                  (T*)hv, (int)s.T, (int)s.M, s.scale,
-                                                 s.scale * 1.4426950408889634f);
+                                                 s.scale * 1.4426950408889634f, hkv_acc, split);
   return launch_status();
 }
 
@@ -465,7 +501,8 @@ int tc_hvp_launch(const CUtensorMap* m, const float* lse, const float* stats, fl
 template <typename T>
 int tc_hvp(const void* q, const void* k, const void* v, const void* w, const float* lse,
            const void* tq, const void* tk, const void* tv, void* hq, void* hk, void* hv,
-           void* o_tan, void* ws, const Shape& s, int dtype, cudaStream_t st) {
+           void* o_tan, void* ws, int64_t ws_bytes, const Shape& s, int dtype,
+           cudaStream_t st) {
   CUtensorMap m[8];
   const int64_t bh = s.B * s.H;
   const void* src[7] = {q, tq, w, k, v, tk, tv};
@@ -478,17 +515,37 @@ int tc_hvp(const void* q, const void* k, const void* v, const void* w, const flo
   // D = 64 adds its hQ tiles through a swizzled fp32 map of the accumulator
   std::memset(&m[7], 0, sizeof(m[7]));
   if (s.D == 64 && !tc::make_map_3d_f32(&m[7], hq_acc, bh, s.T, s.D, 2 * tchvp::BQ)) return -1;
+  // query chunks of the second pass, when the workspace has room for the
+  // fp32 hK/hV partial sums
+  int split = hvp_split(s, sm_count());
+  if (split > 1 && ws_bytes < tc_hvp_ws(s, split)) split = 1;
+  float* hkv_acc = split > 1 ? (float*)((char*)hq_acc + align_up(bh * s.T * s.D * 4)) : nullptr;
+  const int64_t nkv = bh * s.M * s.D;
   int e = tc_jvp<T>(q, k, v, tq, tk, tv, w, lse, o_tan, stats, s, dtype, st);
   if (e != 0) return e;
   const int64_t n = bh * s.T * s.D;
   if (cudaMemsetAsync(hq_acc, 0, n * 4, st) != cudaSuccess) return THERIA_ERR_LAUNCH;
+  if (split > 1 && cudaMemsetAsync(hkv_acc, 0, 2 * nkv * 4, st) != cudaSuccess)
+    return THERIA_ERR_LAUNCH;
+#define THERIA_HVP2(HD, C) \
+  tc_hvp_launch<T, HD, C>(m, lse, stats, hq_acc, hk, hv, hkv_acc, split, s, st)
   if (s.D == 64)
-    e = s.causal ? tc_hvp_launch<T, 64, true>(m, lse, stats, hq_acc, hk, hv, s, st)
-                 : tc_hvp_launch<T, 64, false>(m, lse, stats, hq_acc, hk, hv, s, st);
+    e = s.causal ? THERIA_HVP2(64, true) : THERIA_HVP2(64, false);
   else
-    e = s.causal ? tc_hvp_launch<T, 128, true>(m, lse, stats, hq_acc, hk, hv, s, st)
-                 : tc_hvp_launch<T, 128, false>(m, lse, stats, hq_acc, hk, hv, s, st);
+    e = s.causal ? THERIA_HVP2(128, true) : THERIA_HVP2(128, false);
+#undef THERIA_HVP2
   if (e) return e;
+  if (split > 1) {
+    const unsigned blocks = (unsigned)std::min<int64_t>((nkv / 4 + 255) / 256, 148 * 16);
+    if (hv != nullptr) {
+      tcbwd::finish_kernel<T><<<blocks, 256, 0, st>>>(hkv_acc, (T*)hv, nkv);
+      if (int e2 = launch_status()) return e2;
+    }
+    if (hk != nullptr) {
+      tcbwd::finish_kernel<T><<<blocks, 256, 0, st>>>(hkv_acc + nkv, (T*)hk, nkv);
+      if (int e2 = launch_status()) return e2;
+    }
+  }
   if (hq != nullptr) {
     const unsigned blocks = (unsigned)std::min<int64_t>((n / 4 + 255) / 256, 148 * 16);
     tcbwd::finish_kernel<T><<<blocks, 256, 0, st>>>(hq_acc, (T*)hq, n);
@@ -718,13 +775,13 @@ int theria_sdpa_hvp(const void* q, const void* k, const void* v, const void* w,
   if (small_eligible(s))
     return THERIA_DISPATCH(dtype, small_hvp, q, k, v, w, lse, tq, tk, tv, hq, hk, hv, o_tan, s,
                            st);
-  if (workspace_bytes >= tc_hvp_ws(s) &&
+  if (workspace_bytes >= tc_hvp_ws(s, 1) &&
       use_tc(dtype, s, {q, k, v, w, tq, tk, tv, hq, hk, hv, o_tan})) {
     int e = dtype == THERIA_BF16
                 ? tc_hvp<__nv_bfloat16>(q, k, v, w, lse, tq, tk, tv, hq, hk, hv, o_tan,
-                                        workspace, s, dtype, st)
-                : tc_hvp<__half>(q, k, v, w, lse, tq, tk, tv, hq, hk, hv, o_tan, workspace, s,
-                                 dtype, st);
+                                        workspace, workspace_bytes, s, dtype, st)
+                : tc_hvp<__half>(q, k, v, w, lse, tq, tk, tv, hq, hk, hv, o_tan, workspace,
+                                 workspace_bytes, s, dtype, st);
     if (e >= 0) return e;
   }
   return THERIA_DISPATCH(dtype, simt_hvp, q, k, v, w, lse, tq, tk, tv, hq, hk, hv, o_tan,
