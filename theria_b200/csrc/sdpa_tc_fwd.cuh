@@ -233,7 +233,7 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       for (int i = 0; i < 8; ++i) mp[i] = -INFINITY;
       if (!edge) {
 #pragma unroll
-        for (int i = 0; i < BN; ++i) mp[i & 7] = fmaxf(mp[i & 7], v[i]);
+        for (int i = 0; i < BN; i += 2) mp[(i >> 1) & 7] = tc::max3(mp[(i >> 1) & 7], v[i], v[i + 1]);
       } else {
 #pragma unroll
         for (int i = 0; i < BN; ++i) mp[i & 7] = fmaxf(mp[i & 7], i < lim ? v[i] : -INFINITY);
@@ -271,7 +271,13 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       for (int c = 0; c < BN / 64; ++c) {
         if (!edge) {
 #pragma unroll
-          for (int i = 0; i < 64; ++i) v[c * 64 + i] = tc::ex2(fmaf(v[c * 64 + i], scale_log2, -m_sub));
+          for (int i = 0; i < 64; i += 2) {
+            float x0, x1;
+            tc::fma2(x0, x1, v[c * 64 + i], v[c * 64 + i + 1], scale_log2, scale_log2, -m_sub,
+                     -m_sub);
+            v[c * 64 + i] = tc::ex2(x0);
+            v[c * 64 + i + 1] = tc::ex2(x1);
+          }
         } else {
 #pragma unroll
           for (int i = 0; i < 64; ++i)
@@ -280,7 +286,8 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
         uint32_t pk[32];
 #pragma unroll
         for (int i = 0; i < 64; i += 2) {
-          rs[(i / 2) & 7] += v[c * 64 + i] + v[c * 64 + i + 1];
+          const int k = 2 * ((i >> 1) & 3);  // four chains of paired partial sums
+          tc::add2(rs[k], rs[k + 1], rs[k], rs[k + 1], v[c * 64 + i], v[c * 64 + i + 1]);
           pk[i / 2] = tc::pack2<T>(v[c * 64 + i], v[c * 64 + i + 1]);
         }
         tc::tmem_st32u(t_s + c * 32, pk);
