@@ -317,8 +317,9 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       // Row statistics of this group's 32 queries: one load per lane, then
       // broadcast by shuffles.
       const int ql = q0 + grp * 32 + lane;
-      const float my_l = ql < Tq ? __ldg(lse + row_base + ql) * 1.4426950408889634f : INFINITY;
-      const float my_z = ql < Tq ? __ldg(z + row_base + ql) : 0.f;
+      // negated, so the row terms enter paired adds / fmas directly
+      const float my_l = ql < Tq ? -__ldg(lse + row_base + ql) * 1.4426950408889634f : -INFINITY;
+      const float my_z = ql < Tq ? -__ldg(z + row_base + ql) : 0.f;
       if (!wait(s_full, t & 1)) { ok = false; break; }
       tc::tc_fence_after();
       float s[32], dp[32];
@@ -339,14 +340,22 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       const bool edge = diag || (k0 + BK > M);
       // valid columns e satisfy e >= e_min (causal: query >= key); none if key >= M
       const int e_min = key >= M ? 32 : (diag ? key - (q0 + grp * 32) : 0);
+      // two columns at a time on paired fp32 instructions
 #pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        const float lq = __shfl_sync(0xffffffffu, my_l, e);
-        const float zq = __shfl_sync(0xffffffffu, my_z, e);
-        float p = tc::ex2(fmaf(s[e], scale_log2, -lq));  // rows past the end: lq = +inf -> 0
-        if (edge && e < e_min) p = 0.f;
-        s[e] = p;                   // P^T
-        dp[e] = p * (dp[e] - zq);   // dS^T
+      for (int e = 0; e < 32; e += 2) {
+        const float nl0 = __shfl_sync(0xffffffffu, my_l, e);
+        const float nl1 = __shfl_sync(0xffffffffu, my_l, e + 1);
+        const float nz0 = __shfl_sync(0xffffffffu, my_z, e);
+        const float nz1 = __shfl_sync(0xffffffffu, my_z, e + 1);
+        float x0, x1, g0, g1;
+        tc::fma2(x0, x1, s[e], s[e + 1], scale_log2, scale_log2, nl0, nl1);
+        float p0 = tc::ex2(x0), p1 = tc::ex2(x1);  // rows past the end: -inf -> 0
+        if (edge && e < e_min) p0 = 0.f;
+        if (edge && e + 1 < e_min) p1 = 0.f;
+        s[e] = p0;  // P^T
+        s[e + 1] = p1;
+        tc::add2(g0, g1, dp[e], dp[e + 1], nz0, nz1);
+        tc::mul2(dp[e], dp[e + 1], p0, p1, g0, g1);  // dS^T = P^T (dP^T - z)
       }
       // P^T stays in TMEM as packed 16-bit pairs (A operand of dV += P^T dO);
       // dS^T goes to shared memory (operand of dK and dQ).

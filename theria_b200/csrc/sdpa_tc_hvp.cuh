@@ -287,10 +287,11 @@ hvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       const int q0 = (i_begin + t) * BQ;
       const int ql = q0 + grp * 32 + lane;
       const bool qin = ql < Tq;
-      const float my_l = qin ? __ldg(lse + row_base + ql) * 1.4426950408889634f : INFINITY;
-      const float my_c = qin ? __ldg(stats + row_base + ql) : 0.f;
-      const float my_z = qin ? __ldg(stats + n_rows_total + row_base + ql) : 0.f;
-      const float my_zd = qin ? __ldg(stats + 2 * n_rows_total + row_base + ql) : 0.f;
+      // negated, so the row terms enter paired adds / fmas directly
+      const float my_l = qin ? -__ldg(lse + row_base + ql) * 1.4426950408889634f : -INFINITY;
+      const float my_c = qin ? -__ldg(stats + row_base + ql) : 0.f;
+      const float my_z = qin ? -__ldg(stats + n_rows_total + row_base + ql) : 0.f;
+      const float my_zd = qin ? -__ldg(stats + 2 * n_rows_total + row_base + ql) : 0.f;
       if (!wait(s_full, t & 1)) { ok = false; break; }
       tc::tc_fence_after();
       float sv[32], sd[32], dp[32], dpd[32];
@@ -304,19 +305,31 @@ hvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       const bool diag = CAUSAL && (q0 < k0 + BK);
       const bool edge = diag || (k0 + BK > M);  // uniform per tile
       const int e_min = key >= M ? 32 : (diag ? key - (q0 + grp * 32) : 0);
+      // two columns at a time on paired fp32 instructions
 #pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        const float lq = __shfl_sync(0xffffffffu, my_l, e);
-        const float cq = __shfl_sync(0xffffffffu, my_c, e);
-        const float zq = __shfl_sync(0xffffffffu, my_z, e);
-        const float zdq = __shfl_sync(0xffffffffu, my_zd, e);
-        float p = tc::ex2(fmaf(sv[e], scale_log2, -lq));
-        if (edge && e < e_min) p = 0.f;
-        const float pd = p * (sd[e] * scale - cq);
-        const float g = dp[e] - zq;
-        sv[e] = pd;                                  // Pd^T
-        sd[e] = p * g;                               // dS^T
-        dp[e] = pd * g + p * (dpd[e] - zdq);         // dSd^T
+      for (int e = 0; e < 32; e += 2) {
+        float nl[2], nc[2], nz[2], nzd[2];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          nl[i] = __shfl_sync(0xffffffffu, my_l, e + i);
+          nc[i] = __shfl_sync(0xffffffffu, my_c, e + i);
+          nz[i] = __shfl_sync(0xffffffffu, my_z, e + i);
+          nzd[i] = __shfl_sync(0xffffffffu, my_zd, e + i);
+        }
+        float x0, x1, pd0, pd1, g0, g1, h0, h1;
+        tc::fma2(x0, x1, sv[e], sv[e + 1], scale_log2, scale_log2, nl[0], nl[1]);
+        float p0 = tc::ex2(x0), p1 = tc::ex2(x1);
+        if (edge && e < e_min) p0 = 0.f;
+        if (edge && e + 1 < e_min) p1 = 0.f;
+        tc::fma2(pd0, pd1, sd[e], sd[e + 1], scale, scale, nc[0], nc[1]);
+        tc::mul2(pd0, pd1, p0, p1, pd0, pd1);                       // Pd^T
+        tc::add2(g0, g1, dp[e], dp[e + 1], nz[0], nz[1]);           // dP - z
+        tc::add2(h0, h1, dpd[e], dpd[e + 1], nzd[0], nzd[1]);       // dPd - zdot
+        tc::mul2(sd[e], sd[e + 1], p0, p1, g0, g1);                 // dS^T
+        tc::mul2(h0, h1, p0, p1, h0, h1);
+        tc::fma2(dp[e], dp[e + 1], pd0, pd1, g0, g1, h0, h1);       // dSd^T
+        sv[e] = pd0;
+        sv[e + 1] = pd1;
       }
       // every tile written below was last read by tile t-1's MMAs
       if (t >= 1 && !wait(mma2_done + ((t - 1) & 1), ((t - 1) >> 1) & 1)) { ok = false; break; }

@@ -224,7 +224,7 @@ jvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       return __all_sync(0xffffffffu, tc::mbar_wait(bar, parity, abort));
     };
     const uint32_t a_p = tc::smem_u32(smem + C::oP), a_u = tc::smem_u32(smem + C::oU);
-    float c_acc = 0.f;
+    float c_pair[2] = {0.f, 0.f};
     for (int j = 0; j < n_tiles; ++j) {
       if (!wait(s_full, j & 1)) { ok = false; break; }
       tc::tc_fence_after();
@@ -246,16 +246,24 @@ jvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       // masking only where a tile crosses the causal diagonal or the last key
       const bool edge = (col0 + HALF > M) || (CAUSAL && col0 + HALF - 1 > q0);
       const int lim = (CAUSAL ? min(M, row + 1) : M) - col0;  // valid: e < lim
+      // two columns at a time on paired fp32 instructions
 #pragma unroll
-      for (int e = 0; e < HALF; ++e) {
-        float p = tc::ex2(fmaf(sv[e], scale_log2, -lse2));
-        if (edge && e >= lim) p = 0.f;
+      for (int e = 0; e < HALF; e += 2) {
+        float x0, x1, a0, a1, u0, u1;
+        tc::fma2(x0, x1, sv[e], sv[e + 1], scale_log2, scale_log2, -lse2, -lse2);
+        float p0 = tc::ex2(x0), p1 = tc::ex2(x1);
+        if (edge && e >= lim) p0 = 0.f;
+        if (edge && e + 1 >= lim) p1 = 0.f;
+        tc::mul2(a0, a1, sd[e], sd[e + 1], scale, scale);
+        tc::mul2(a0, a1, p0, p1, a0, a1);
         // c is summed from U as rounded for the MMA, so that OA - c OP
         // cancels consistently (a row with one key gives Odot = tV exactly).
-        const float u = to_f32<T>(from_f32<T>(p * (sd[e] * scale)));
-        c_acc += u;
-        sv[e] = p;
-        sd[e] = u;
+        tc::unpack2<T>(tc::pack2<T>(a0, a1), u0, u1);
+        tc::add2(c_pair[0], c_pair[1], c_pair[0], c_pair[1], u0, u1);
+        sv[e] = p0;
+        sv[e + 1] = p1;
+        sd[e] = u0;
+        sd[e + 1] = u1;
       }
       // P / U tiles were read by tile j-1's MMAs.
       if (j >= 1 && !wait(pv_done, (j - 1) & 1)) { ok = false; break; }
@@ -276,7 +284,7 @@ jvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
     }
     // ------------------------------------------------------------ epilogue
     // c = rowsum(P Sd) over both groups' columns.
-    atomicAdd(stat_s + r, c_acc);
+    atomicAdd(stat_s + r, c_pair[0] + c_pair[1]);
     tc::mbar_arrive(c_ready);
     if (ok) ok = wait(c_ready, 0);
     if (ok) ok = wait(pv_done, (n_tiles - 1) & 1);

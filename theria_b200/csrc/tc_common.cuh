@@ -341,6 +341,19 @@ template <> __device__ __forceinline__ uint32_t pack2<__half>(float a, float b) 
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// The two floats of a packed 16-bit pair (inverse of pack2).
+template <typename T> __device__ __forceinline__ void unpack2(uint32_t p, float& a, float& b);
+template <> __device__ __forceinline__ void unpack2<__nv_bfloat16>(uint32_t p, float& a,
+                                                                   float& b) {
+  a = __uint_as_float(p << 16);
+  b = __uint_as_float(p & 0xffff0000u);
+}
+template <> __device__ __forceinline__ void unpack2<__half>(uint32_t p, float& a, float& b) {
+  const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&p));
+  a = f.x;
+  b = f.y;
+}
+
 template <typename T> struct AbFmt;
 template <> struct AbFmt<__nv_bfloat16> { static constexpr int v = 1; };
 template <> struct AbFmt<__half> { static constexpr int v = 0; };
@@ -367,6 +380,14 @@ __device__ __forceinline__ void add2(float& d0, float& d1, float a0, float a1, f
   asm("{.reg .b64 ra, rb, rd;\n\t"
       "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
       "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+__device__ __forceinline__ void mul2(float& d0, float& d1, float a0, float a1, float b0,
+                                     float b1) {
+  asm("{.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;}"
       : "=f"(d0), "=f"(d1)
       : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
 }
