@@ -26,7 +26,7 @@ from __future__ import annotations
 
 import torch
 
-from theria_b200.attention.fused import SDPAFunction
+from theria_b200.attention.fused import sdpa_apply
 from theria_b200.attention.reference import reference_attention
 from theria_b200.attention.triton_qk import triton_qk, triton_qk_fast, triton_qk_softmax
 from theria_b200.autograd.sdpa_custom_function import SDPACustom
@@ -50,7 +50,7 @@ def sdpa_custom(q, k, v, *, backend: str = "triton_full_fused", causal: bool = F
     if backend == "custom":
         return SDPACustom.apply(q, k, v, causal)
     if backend in FUSED_BACKENDS:
-        return SDPAFunction.apply(q, k, v, causal, None)
+        return sdpa_apply(q, k, v, causal, None)
     if backend == "reference":
         return reference_attention(q, k, v)
     if backend == "triton_qk_softmax":

@@ -105,14 +105,49 @@ class SDPAFunction(torch.autograd.Function):
 TritonFusedSDPAFunction = SDPAFunction
 
 
+def _padded_head_dim(q, d):
+    # 16-bit inputs pad to the tensor-core head dims, others to the larger dim
+    if q.dtype in (torch.float16, torch.bfloat16):
+        for cand in (64, 128):
+            if d <= cand:
+                return cand
+    return d
+
+
+def sdpa_apply(q, k, v, causal: bool = False, scale=None):
+    """SDPAFunction with a value head dim Dv that may differ from D.
+
+    The kernels take one head dim for q, k and v.  For Dv != D the smaller
+    side is padded with zero columns to a common width (for 16-bit inputs
+    the next tensor-core width, 64 or 128): zero columns of q and k leave the
+    scores unchanged (the scale stays 1/sqrt(D) of the real D), zero columns
+    of v add zero output columns, and the output is sliced back to Dv.  Pad
+    and slice are linear, so first and second derivatives and forward-mode
+    tangents pass through them exactly.  This generalises the reference,
+    whose fused path asserts Dv == D (``theria/attention/triton_qk.py:318``)
+    and lists Dv != D as future work.
+    """
+    D, Dv = q.shape[-1], v.shape[-1]
+    if Dv == D:
+        return SDPAFunction.apply(q, k, v, causal, scale)
+    scale = ops.default_scale(q) if scale is None else float(scale)
+    Dp = _padded_head_dim(q, max(D, Dv))
+    pad = torch.nn.functional.pad
+    if Dp > D:
+        q, k = pad(q, (0, Dp - D)), pad(k, (0, Dp - D))
+    if Dp > Dv:
+        v = pad(v, (0, Dp - Dv))
+    return SDPAFunction.apply(q, k, v, causal, scale)[..., :Dv]
+
+
 def sdpa_fused(q, k, v, causal: bool = False, scale=None):
-    """Differentiable fused SDPA returning q.dtype."""
-    return SDPAFunction.apply(q, k, v, causal, scale)
+    """Differentiable fused SDPA returning q.dtype (Dv may differ from D)."""
+    return sdpa_apply(q, k, v, causal, scale)
 
 
 def triton_sdpa_fused_autograd(q, k, v, causal: bool = False):
     """Reference name (triton_qk.py:390-391)."""
-    return SDPAFunction.apply(q, k, v, causal, None)
+    return sdpa_apply(q, k, v, causal, None)
 
 
 def triton_sdpa_fused(q, k, v, return_stats: bool = False, causal: bool = False):

@@ -5,12 +5,12 @@ In the reference ``SDPAFunction`` is the documented *failing* boundary
 twice-differentiable fused function, so ``sdpa`` supports grad-of-grad.
 """
 
-from theria_b200.attention.fused import SDPAFunction
+from theria_b200.attention.fused import SDPAFunction, sdpa_apply
 
 
 def sdpa(q, k, v, causal: bool = False):
-    """Public SDPA entry point: inputs (B, H, T, D), output (B, H, T, D)."""
-    return SDPAFunction.apply(q, k, v, causal, None)
+    """Public SDPA entry point: q, k (B, H, T|M, D), v (B, H, M, Dv) -> (B, H, T, Dv)."""
+    return sdpa_apply(q, k, v, causal, None)
 
 
 __all__ = ["SDPAFunction", "sdpa"]
