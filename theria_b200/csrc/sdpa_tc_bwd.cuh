@@ -61,8 +61,8 @@ struct Smem {
   static constexpr int oStage = oDS + 2 * kP;
   static constexpr int oBar = oStage + kStage;
   // kv_full, q_full[4], q_empty[4], s_full, s_read, p_full[2], mma2_done[2],
-  // dq_free[2], drain[2], stage_free, stage_full
-  static constexpr int nBar = 1 + 8 + 2 + 6 + 2 + 2;
+  // dq_free[2], drain[2], stage_free, stage_full, kv_tmem
+  static constexpr int nBar = 1 + 8 + 2 + 6 + 2 + 2 + 1;
   static constexpr int oTmem = oBar + nBar * 8;
   static constexpr int oAbort = oTmem + 4;
   static constexpr int kBytes = oAbort + 4;
@@ -134,6 +134,7 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
   uint64_t* drain = bars + 17;      // [2] each issuer's last MMAs done
   uint64_t* stage_free = bars + 19; // dQ staging buffer read by the previous reduction
   uint64_t* stage_full = bars + 20; // dQ staging buffer written (128 arrivals)
+  uint64_t* kv_tmem = bars + 21;    // D = 64: K and V copied into TMEM (256 arrivals)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::oTmem);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + L::oAbort);
 
@@ -164,6 +165,7 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
     tc::mbar_init(drain + 1, 1);
     tc::mbar_init(stage_free, 1);
     tc::mbar_init(stage_full, NDQ);
+    tc::mbar_init(kv_tmem, NCOMPUTE);
     *abort = 0;
     tc::fence_barrier_init();
   }
@@ -177,6 +179,10 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
   // 16-bit P^T buffers [448+32b, 480+32b).
   const uint32_t t_dv = tmem + 128, t_dk = tmem + 128 + HD, t_dqp = tmem + 256;
   const uint32_t t_dqt = tmem + 384, t_pt = tmem + 448;
+  // D = 64: K and V as TMEM A operands of S^T and dP^T (packed 16-bit pairs,
+  // lane = key, 32 columns each): they are read by every tile's products,
+  // and from TMEM they no longer take shared-memory bandwidth.
+  const uint32_t t_kt = tmem + 320, t_vt = tmem + 352;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -223,6 +229,7 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
         // which is free once the compute warps loaded the previous tile.
         const uint64_t kK = tc::sw128_desc(a_k, 16, 1024), kV = tc::sw128_desc(a_v, 16, 1024);
         const uint64_t kQ = tc::sw128_desc(a_q, 16, 1024), kDO = tc::sw128_desc(a_do, 16, 1024);
+        if (kPairDq) ok = ok && tc::mbar_wait(kv_tmem, 0, abort);
         for (int t = 0; ok && t < n_iter; ++t) {
           const int st = t % QST;
           if (!tc::mbar_wait(q_full + st, (t / QST) & 1, abort)) break;
@@ -232,10 +239,16 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
           for (int kk = 0; kk < HD / 16; ++kk) {
             const uint32_t off_a = (kk / 4) * (BK * 128) + (kk % 4) * 32;
             const uint32_t off_b = st * L::kQ + (kk / 4) * (BQ * 128) + (kk % 4) * 32;
-            tc::mma_ss(tmem + 64, tc::desc_at(kV, off_a), tc::desc_at(kDO, off_b), id_s,
-                       kk > 0 ? 1u : 0u);
-            tc::mma_ss(tmem, tc::desc_at(kK, off_a), tc::desc_at(kQ, off_b), id_s,
-                       kk > 0 ? 1u : 0u);
+            if constexpr (kPairDq) {
+              tc::mma_ts(tmem + 64, t_vt + kk * 8, tc::desc_at(kDO, off_b), id_s,
+                         kk > 0 ? 1u : 0u);
+              tc::mma_ts(tmem, t_kt + kk * 8, tc::desc_at(kQ, off_b), id_s, kk > 0 ? 1u : 0u);
+            } else {
+              tc::mma_ss(tmem + 64, tc::desc_at(kV, off_a), tc::desc_at(kDO, off_b), id_s,
+                         kk > 0 ? 1u : 0u);
+              tc::mma_ss(tmem, tc::desc_at(kK, off_a), tc::desc_at(kQ, off_b), id_s,
+                         kk > 0 ? 1u : 0u);
+            }
           }
           tc::mma_commit(s_full);
         }
@@ -311,7 +324,28 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
     };
     const uint32_t a_ds = tc::smem_u32(smem + L::oDS);
     const size_t row_base = (size_t)bh * Tq;
-    for (int t = 0; t < n_iter; ++t) {
+    if (kPairDq && n_iter > 0) {
+      // copy this thread's key row of K (group 0) or V (group 1) into TMEM:
+      // the 128-byte SW128 row is 32 packed pairs, one per column
+      ok = wait(kv_full, 0);
+      if (ok) {
+        const uint32_t row = tc::smem_u32(smem + (grp == 0 ? L::oK : L::oV)) + (uint32_t)r * 128;
+        uint32_t w[32];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const float4 x = tc::ld_shared_f4(row + (uint32_t)((c ^ (r & 7)) << 4));
+          w[4 * c] = __float_as_uint(x.x);
+          w[4 * c + 1] = __float_as_uint(x.y);
+          w[4 * c + 2] = __float_as_uint(x.z);
+          w[4 * c + 3] = __float_as_uint(x.w);
+        }
+        tc::tmem_st32u((grp == 0 ? t_kt : t_vt) + lane_off, w);
+        tc::tmem_wait_st();
+        tc::tc_fence_before();
+        tc::mbar_arrive(kv_tmem);
+      }
+    }
+    for (int t = 0; ok && t < n_iter; ++t) {
       const int b = t & 1;
       const int q0 = tile_of(t) * BQ;
       // Row statistics of this group's 32 queries: one load per lane, then
