@@ -412,7 +412,7 @@ def run_strong_split(args, world, rank, dev, peak):
             tf = flops(kind, B, H, N, D) / (ms * 1e-3) / 1e12
             out[kind + "_ms"] = ms
             out[kind + "_tflops"] = tf
-            out[kind + "_frac"] = tf / peak
+            out[kind + "_frac"] = tf / (peak * world)  # per GPU, of one GPU's peak
         res[name] = out
         del q, k, v, w, tq, tk, tv, lse
     torch.cuda.empty_cache()
@@ -484,7 +484,7 @@ def run_sweep(args, world, rank, dev, peak, points=None):
                   "hvp_tflops": f("hvp", t_h), "fwd_ms": t_f, "bwd_ms": t_b,
                   "jvp_ms": t_j, "hvp_ms": t_h}
             for kind in ("fwd", "fwdbwd", "jvp", "hvp"):
-                pt[kind + "_frac"] = pt[kind + "_tflops"] / peak
+                pt[kind + "_frac"] = pt[kind + "_tflops"] / (peak * world)  # per GPU
             out.append(pt)
             del q, k, v, w, tq, tk, tv, o, lse
     torch.cuda.empty_cache()
