@@ -75,24 +75,42 @@ __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float 
                : "memory");
 }
 
-// z = rowsum(dO * O) (O in o_dtype) and zero the fp32 dQ accumulator; one
-// warp per row.
+// z = rowsum(dO * O) (O in o_dtype) and zero the fp32 dQ accumulator.
+// D / 8 threads per row (D in {64, 128}), each on 8 consecutive elements with
+// 16-byte loads and stores; the row sum is finished by shuffles among them.
 template <typename T>
 __global__ void __launch_bounds__(256)
 prep_kernel(const void* __restrict__ o, int o_f32, const T* __restrict__ dout,
             float* __restrict__ z, float* __restrict__ dq_acc, int64_t rows, int D) {
-  const int lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
-  if (row >= rows) return;
+  const int tpr = D / 8;
+  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t row = gid / tpr;
+  const int part = (int)(gid % tpr);
   float a = 0.f;
-  for (int d = lane; d < D; d += 32) {
-    const float ov = o_f32 ? static_cast<const float*>(o)[row * D + d]
-                           : to_f32<T>(static_cast<const T*>(o)[row * D + d]);
-    a = fmaf(to_f32<T>(dout[row * D + d]), ov, a);
-    dq_acc[row * D + d] = 0.f;
+  if (row < rows) {
+    const int64_t base = row * D + part * 8;
+    const uint4 dr = *reinterpret_cast<const uint4*>(dout + base);
+    const T* dv = reinterpret_cast<const T*>(&dr);
+    float ov[8];
+    if (o_f32) {
+      const float4 x = *reinterpret_cast<const float4*>(static_cast<const float*>(o) + base);
+      const float4 y = *reinterpret_cast<const float4*>(static_cast<const float*>(o) + base + 4);
+      ov[0] = x.x; ov[1] = x.y; ov[2] = x.z; ov[3] = x.w;
+      ov[4] = y.x; ov[5] = y.y; ov[6] = y.z; ov[7] = y.w;
+    } else {
+      const uint4 orr = *reinterpret_cast<const uint4*>(static_cast<const T*>(o) + base);
+      const T* op = reinterpret_cast<const T*>(&orr);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ov[i] = to_f32<T>(op[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) a = fmaf(to_f32<T>(dv[i]), ov[i], a);
+    const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+    *reinterpret_cast<float4*>(dq_acc + base) = zero;
+    *reinterpret_cast<float4*>(dq_acc + base + 4) = zero;
   }
-  a = warp_sum(a);
-  if (lane == 0) z[row] = a;
+  for (int off = tpr / 2; off > 0; off >>= 1) a += __shfl_xor_sync(0xffffffffu, a, off);
+  if (row < rows && part == 0) z[row] = a;
 }
 
 // dQacc (already scaled) -> dQ in the input dtype.

@@ -367,7 +367,7 @@ int tc_bwd(const void* q, const void* k, const void* v, const void* o, int o_dty
   std::memset(&mdq, 0, sizeof(mdq));
   if (s.D == 64 && !tc::make_map_3d_f32(&mdq, dq_acc, bh, s.T, s.D, 2 * tcbwd::BQ)) return -1;
   if (o != nullptr) {
-    tcbwd::prep_kernel<T><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(
+    tcbwd::prep_kernel<T><<<(unsigned)((rows * (s.D / 8) + 255) / 256), 256, 0, st>>>(
         o, o_dtype == THERIA_F32, (const T*)dout, z, dq_acc, rows, (int)s.D);
     if (int e = launch_status()) return e;
   } else {
