@@ -194,3 +194,31 @@ def test_forward_mode_ad_uses_the_jvp_kernel(causal, shape):
         primal, tangent = fwAD.unpack_dual(out)
     assert max_rel(primal, orc.attention(q, k, v, causal=causal)) <= 1e-5
     assert max_rel(tangent, orc.jvp(q, k, v, tq, tk, tv, causal=causal)) <= 1e-5
+
+
+def test_three_call_backward_computes_once():
+    # the reference's pattern: sdpa_bwd_dq, _dk, _dv on the same inputs
+    from theria_b200 import _lib
+    from theria_b200.attention.triton_sdpa_backward import sdpa_bwd_dk, sdpa_bwd_dq, sdpa_bwd_dv
+    g = torch.Generator("cpu").manual_seed(9)
+    q, k, v, do = (torch.randn(2, 2, 200, 64, generator=g).to(torch.bfloat16).cuda()
+                   for _ in range(4))
+    scale = 64 ** -0.5
+    s = torch.matmul(q.float(), k.float().transpose(-2, -1)) * scale
+    m = s.max(dim=-1).values
+    l = torch.exp(s - m.unsqueeze(-1)).sum(dim=-1)
+    lib = _lib.load()
+    n0 = lib.theria_launch_count()
+    dq = sdpa_bwd_dq(q, k, v, do, m, l, scale)
+    n1 = lib.theria_launch_count()
+    dk = sdpa_bwd_dk(q, k, v, do, m, l, scale)
+    dv = sdpa_bwd_dv(q, k, do, m, l, scale)
+    assert n1 > n0 and lib.theria_launch_count() == n1  # dk, dv: no new launches
+    ref = orc.backward(q.float().cpu(), k.float().cpu(), v.float().cpu(), do.float().cpu())
+    for x, r in zip((dq, dk, dv), ref):
+        assert (x.float().cpu() - r).abs().max().item() <= 2e-2
+    # a modified input is never served from the kept results
+    do.mul_(2.0)
+    dk2 = sdpa_bwd_dk(q, k, v, do, m, l, scale)
+    assert lib.theria_launch_count() > n1
+    assert (dk2.float().cpu() - 2 * ref[1]).abs().max().item() <= 4e-2

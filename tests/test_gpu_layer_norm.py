@@ -125,3 +125,29 @@ def test_gelu_second_derivative_matches_torch():
     for a, b in zip(run(gelu, "cuda", torch.float32),
                     run(torch.nn.functional.gelu, "cpu", torch.float64)):
         assert _rel(a, b) <= 1e-5
+
+
+def test_layer_norm_single_task_with_degenerate_row_strides():
+    # one task: affine rows taken from a transposed [D, 1] view have row
+    # stride 1 < D (torch still calls them contiguous); only row 0 is read,
+    # so the kernels must accept them (first and second derivatives)
+    D = 64
+    g = torch.Generator("cpu").manual_seed(5)
+    x = (torch.randn(1, 7, D, generator=g) * 2).double()
+    wcol = (1 + 0.3 * torch.randn(D, 1, generator=g)).double()
+    bcol = torch.randn(D, 1, generator=g).double()
+    r, vx = torch.randn(1, 7, D, generator=g).double(), torch.randn(1, 7, D, generator=g).double()
+    outs = []
+    for dev, fn in (("cuda", layer_norm), ("cpu", layer_norm_reference)):
+        xd = x.to(dev).float().requires_grad_(True) if dev == "cuda" else x.clone().requires_grad_(True)
+        wd = (wcol.to(dev).float() if dev == "cuda" else wcol.clone()).requires_grad_(True)
+        bd = (bcol.to(dev).float() if dev == "cuda" else bcol.clone()).requires_grad_(True)
+        w, b = wd.t(), bd.t()  # [1, D] views with stride (1, 1)
+        assert w.stride() == (1, 1)
+        y = fn(xd, w, b)
+        gx, gw, gb = torch.autograd.grad((y * r.to(dev).to(y.dtype)).sum(), (xd, w, b),
+                                         create_graph=True)
+        l2 = (gx * vx.to(dev).to(gx.dtype)).sum() + gw.sum() + gb.sum()
+        outs.append([y, gx, gw, gb] + list(torch.autograd.grad(l2, (xd, wd))))
+    for a, b in zip(*outs):
+        assert _rel(a, b.double()) <= 1e-4

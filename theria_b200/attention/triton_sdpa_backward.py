@@ -71,24 +71,56 @@ def _cast(t, dtype):
     return t if t.dtype == dtype else t.to(dtype)
 
 
+# The reference's callers obtain a backward as three calls on the same
+# inputs (sdpa_bwd_dq, sdpa_bwd_dk, sdpa_bwd_dv; ``theria/attention/
+# triton_qk.py:384-386``, ``hvp_utils.py:22-26``).  One kernel call yields all
+# three gradients at the cost of one, so the first call of such a sequence
+# computes all three and keeps the two not asked for; a later call with the
+# very same tensor objects, unmodified (version counters unchanged), takes
+# its gradient from there, once.  The entry holds references to its inputs,
+# so their memory cannot be reused while it lives; any other call replaces
+# it.
+_pending = {}
+
+
+def _key(*ts):
+    return tuple((id(t), t._version) for t in ts)
+
+
+def _take(kind, base, v):
+    if _pending.get("base") == base and (v is None or _pending.get("v") == v):
+        got = _pending["grads"].pop(kind, None)
+        if not _pending["grads"]:
+            _pending.clear()  # all handed out: release the inputs
+        return got
+    return None
+
+
+def _all_three(q, k, v, dout, m, l, scale, causal):
+    dt = q.dtype
+    dq, dk, dv = ops.backward(q, _cast(k, dt), _cast(v, dt), _cast(dout, dt).contiguous(),
+                              ops.lse_from_ml(m, l), causal=causal, scale=float(scale))
+    _pending.clear()
+    _pending.update(base=_key(q, k, dout, m, l) + ((float(scale), bool(causal)),),
+                    v=_key(v), grads={"dq": dq, "dk": dk.to(k.dtype), "dv": dv},
+                    refs=(q, k, v, dout, m, l))
+    return _pending["grads"]
+
+
 def sdpa_bwd_dq(q, k, v, dout, m, l, scale, causal: bool = False):
     """dQ = scale * [P * (dP - z)] K, in q.dtype."""
     _assert_backward_contract(q, k, v, dout, m, l)
-    dt = q.dtype
-    dq, _, _ = ops.backward(q, _cast(k, dt), _cast(v, dt), _cast(dout, dt).contiguous(),
-                            ops.lse_from_ml(m, l), causal=causal, scale=float(scale),
-                            need=(True, False, False))
-    return dq
+    base = _key(q, k, dout, m, l) + ((float(scale), bool(causal)),)
+    got = _take("dq", base, _key(v))
+    return got if got is not None else _all_three(q, k, v, dout, m, l, scale, causal).pop("dq")
 
 
 def sdpa_bwd_dk(q, k, v, dout, m, l, scale, causal: bool = False):
     """dK = scale * dS^T Q, in k.dtype."""
     _assert_backward_contract(q, k, v, dout, m, l)
-    dt = q.dtype
-    _, dk, _ = ops.backward(q, _cast(k, dt), _cast(v, dt), _cast(dout, dt).contiguous(),
-                            ops.lse_from_ml(m, l), causal=causal, scale=float(scale),
-                            need=(False, True, False))
-    return dk.to(k.dtype)
+    base = _key(q, k, dout, m, l) + ((float(scale), bool(causal)),)
+    got = _take("dk", base, _key(v))
+    return got if got is not None else _all_three(q, k, v, dout, m, l, scale, causal).pop("dk")
 
 
 def sdpa_bwd_dv(q, k, dout, m, l, scale, causal: bool = False):
@@ -99,6 +131,10 @@ def sdpa_bwd_dv(q, k, dout, m, l, scale, causal: bool = False):
     dQ/dK terms that this call does not store.
     """
     _assert_backward_contract(q, k, None, dout, m, l, require_v=False)
+    # dV does not depend on V: any pending sequence on these inputs serves
+    got = _take("dv", _key(q, k, dout, m, l) + ((float(scale), bool(causal)),), None)
+    if got is not None:
+        return got
     dt = q.dtype
     kk = _cast(k, dt)
     _, _, dv = ops.backward(q, kk, kk, _cast(dout, dt).contiguous(), ops.lse_from_ml(m, l),

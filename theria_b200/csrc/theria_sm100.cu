@@ -389,7 +389,7 @@ int tc_bwd(const void* q, const void* k, const void* v, const void* o, int o_dty
   if (e) return e;
   if (dq != nullptr) {
     const int64_t n = rows * s.D;
-    const unsigned blocks = (unsigned)std::min<int64_t>((n / 4 + 255) / 256, 148 * 16);
+    const unsigned blocks = (unsigned)std::min<int64_t>((n / 8 + 255) / 256, 148 * 16);
     tcbwd::finish_kernel<T><<<blocks, 256, 0, st>>>(dq_acc, (T*)dq, n);
     return launch_status();
   }
@@ -536,7 +536,7 @@ int tc_hvp(const void* q, const void* k, const void* v, const void* w, const flo
 #undef THERIA_HVP2
   if (e) return e;
   if (split > 1) {
-    const unsigned blocks = (unsigned)std::min<int64_t>((nkv / 4 + 255) / 256, 148 * 16);
+    const unsigned blocks = (unsigned)std::min<int64_t>((nkv / 8 + 255) / 256, 148 * 16);
     if (hv != nullptr) {
       tcbwd::finish_kernel<T><<<blocks, 256, 0, st>>>(hkv_acc, (T*)hv, nkv);
       if (int e2 = launch_status()) return e2;
@@ -547,7 +547,7 @@ int tc_hvp(const void* q, const void* k, const void* v, const void* w, const flo
     }
   }
   if (hq != nullptr) {
-    const unsigned blocks = (unsigned)std::min<int64_t>((n / 4 + 255) / 256, 148 * 16);
+    const unsigned blocks = (unsigned)std::min<int64_t>((n / 8 + 255) / 256, 148 * 16);
     tcbwd::finish_kernel<T><<<blocks, 256, 0, st>>>(hq_acc, (T*)hq, n);
     return launch_status();
   }
