@@ -83,6 +83,11 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
   const int q0 = cta * (NQT * BM);
   int n_tiles = (M + BN - 1) / BN;
   if (CAUSAL) n_tiles = min(n_tiles, (q0 + NQT * BM - 1) / BN + 1);
+  // Key tiles query tile t needs: causal, the first tile stops one key
+  // tile before the second (that tile would be masked out entirely).
+  auto tiles_of = [&](int t) {
+    return CAUSAL ? min(n_tiles, (q0 + t * BM + BM - 1) / BN + 1) : n_tiles;
+  };
 
   if (threadIdx.x == 0) {
     tc::mbar_init(q_full, 1);
@@ -184,16 +189,19 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
         if (more && !tc::mbar_wait(k_full + (j + 1) % STAGES, ((j + 1) / STAGES) & 1, abort))
           break;
         for (int t = 0; t < NQT; ++t) {
-          if (!tc::mbar_wait(p_full + t, j & 1, abort)) { ok = false; break; }
-          tc::tc_fence_after();
-          // O_t += P_t V_j, P_t read from TMEM (packed pairs, 8 columns per 16 keys)
+          const int nt = tiles_of(t);
+          if (j < nt) {
+            if (!tc::mbar_wait(p_full + t, j & 1, abort)) { ok = false; break; }
+            tc::tc_fence_after();
+            // O_t += P_t V_j, P_t read from TMEM (packed pairs, 8 columns per 16 keys)
 #pragma unroll
-          for (int kk = 0; kk < BN / 16; ++kk)
-            tc::mma_ts(tmem + 256 + t * HD, tmem + t * 128 + kk * 8, tc::desc_at(dv, kk * 2048),
-                       id_pv, (j > 0 || kk > 0) ? 1u : 0u);
-          if (!more) tc::mma_commit(o_done + t);
+            for (int kk = 0; kk < BN / 16; ++kk)
+              tc::mma_ts(tmem + 256 + t * HD, tmem + t * 128 + kk * 8,
+                         tc::desc_at(dv, kk * 2048), id_pv, (j > 0 || kk > 0) ? 1u : 0u);
+            if (j + 1 == nt) tc::mma_commit(o_done + t);
+          }
           if (t == NQT - 1) tc::mma_commit(v_empty + st);
-          if (more) issue_s(t, j + 1);
+          if (j + 1 < nt) issue_s(t, j + 1);
         }
       }
       // Every MMA issued above completes before TMEM is freed.
@@ -215,7 +223,8 @@ fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
     auto wait = [&](uint64_t* bar, uint32_t parity) {
       return __all_sync(0xffffffffu, tc::mbar_wait(bar, parity, abort));
     };
-    for (int j = 0; j < n_tiles; ++j) {
+    const int nt = tiles_of(t);
+    for (int j = 0; j < nt; ++j) {
       if (!wait(s_full + t, j & 1)) { ok = false; break; }
       tc::tc_fence_after();
       const int col0 = j * BN;
