@@ -146,3 +146,22 @@ def test_device_error_word_is_clear():
     s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     assert lib.theria_get_device_error(ctypes.byref(flag), s) == 0
     assert flag.value == 0
+
+
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("T", [16384 + 64, 1000])
+@pytest.mark.parametrize("causal", [False, True])
+def test_backward_long_query_heads_with_few_keys(D, T, causal):
+    # Query heads longer than the longest configs[4] point (T = 16448) and
+    # ragged ones, against few keys (the oracle stays cheap): every query
+    # unit's fp32 dQ accumulator collects the contributions of all key tiles
+    # that see it; two calls in a row start from fresh workspaces.
+    M = 200
+    (q, do, _, _), (k, v, _, _, _) = _draw((1, 1, T, D), (1, 1, M, D), torch.bfloat16, seed=3)
+    qd, kd, vd, dod = (t.to(DEV) for t in (q, k, v, do))
+    o, lse = ops.forward(qd, kd, vd, causal=causal)
+    ref = orc.backward(q.float(), k.float(), v.float(), do.float(), causal=causal)
+    for _ in range(2):
+        dq, dk, dv = ops.backward(qd, kd, vd, dod, lse, o=o, causal=causal)
+        for x, r in zip((dq, dk, dv), ref):
+            _check(x, r, torch.bfloat16)
