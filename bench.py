@@ -263,18 +263,20 @@ def run_fwdbwd(args, world, rank, dev, causal=False, with_e2e=True, dt=torch.bfl
     out = {"ms_per_step": ms, "value": f / (ms * 1e-3) / 1e12,
            "gpu_launches": launches, "clocks": clk.summary()}
 
-    # per-launch split of the step (same stream, CUDA events) for the roofline
-    t_f, t_b = [], []
-    for _ in range(3):
-        e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    # per-launch split of the step (same stream, CUDA events) for the roofline;
+    # a step queued ahead keeps the device busy, so no interval includes the
+    # host's launch latency
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(5)]
+    step()
+    for e in evs:
         e[0].record()
         o, lse = ops.forward(q, k, v, causal=causal)
         e[1].record()
         ops.backward(q, k, v, do, lse, o=o, causal=causal)
         e[2].record()
-        torch.cuda.synchronize()
-        t_f.append(e[0].elapsed_time(e[1]))
-        t_b.append(e[1].elapsed_time(e[2]))
+    torch.cuda.synchronize()
+    t_f = [e[0].elapsed_time(e[1]) for e in evs]
+    t_b = [e[1].elapsed_time(e[2]) for e in evs]
     out["t_fwd_ms"] = statistics.median(t_f)
     out["t_bwd_ms"] = statistics.median(t_b)
     out["fwd_tflops"] = flops("fwd", B, H, N, D, causal) / (out["t_fwd_ms"] * 1e-3) / 1e12

@@ -19,9 +19,11 @@
 // double buffer [384 + 64b, 448 + 64b); for D = 64 as dQ = dS K for a PAIR of
 // query tiles at once (M = 128 query rows, the two adjacent dS^T buffers read
 // as one MN-major operand) into [256, 320).
-// Warp roles: warp 0 TMA; warp 1 issues S^T/dP^T and owns TMEM; warp 2
-// issues dV/dK/dQ; warps 3..10 two groups of four (one per TMEM lane quarter)
-// splitting the columns; warps 11..14 flush dQ.  Two issuing threads: one
+// Warp roles: warp 0 TMA (for D = 64 non-causal also each tile's row terms
+// LSE and z, staged in shared memory for broadcast loads); warp 1
+// issues S^T/dP^T and owns TMEM; warp 2 issues dV/dK/dQ; warps 3..10 two
+// groups of four (one per TMEM lane quarter) splitting the columns; warps
+// 11..14 flush dQ.  Two issuing threads: one
 // thread issues a tcgen05.mma only every ~60 cycles, slower than the tensor
 // core runs the N = 64 products, and each barrier wait between groups stalls
 // its issue stream; with the two groups on separate threads each hides the
@@ -59,7 +61,10 @@ struct Smem {
   static constexpr int oDO = oQ + QST * kQ; // QST stages
   static constexpr int oDS = oDO + QST * kQ;  // 2 buffers (adjacent: a pair is one M=128 operand)
   static constexpr int oStage = oDS + 2 * kP;
-  static constexpr int oBar = oStage + kStage;
+  // per Q/dO stage: the row terms {-LSE*log2(e), -z} of the tile's 64 queries
+  static constexpr int kRow = BQ * 8;
+  static constexpr int oRow = oStage + kStage;
+  static constexpr int oBar = oRow + QST * kRow;
   // kv_full, q_full[4], q_empty[4], s_full, s_read, p_full[2], mma2_done[2],
   // dq_free[2], drain[2], stage_free, stage_full, kv_tmem
   static constexpr int nBar = 1 + 8 + 2 + 6 + 2 + 2 + 1;
@@ -138,13 +143,19 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
            float scale, float scale_log2) {
   using L = Smem<HD>;
   constexpr bool kPairDq = (HD == 64);  // dQ per pair of query tiles (see header)
+  // The compute warps take each query's row terms (LSE, z) from a copy the
+  // producer warp stages in shared memory (broadcast loads) for D = 64
+  // non-causal, where they were issue-bound on the per-query shuffles
+  // (+9 %); elsewhere from shuffles of one load per lane, which keep the
+  // shared-memory pipe (the D = 128 limit) free and measured faster.
+  constexpr bool kRowStage = (HD == 64) && !CAUSAL;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::oBar);
   uint64_t* kv_full = bars;
   constexpr int QST = L::QST;
-  uint64_t* q_full = bars + 1;      // [QST] Q_t and dO_t landed
+  uint64_t* q_full = bars + 1;      // [QST] Q_t, dO_t and the tile's row terms landed
   uint64_t* q_empty = bars + 5;     // [QST] stage free (MMAs reading it done)
   uint64_t* s_full = bars + 9;      // S^T, dP^T of the current tile computed
   uint64_t* s_read = bars + 10;     // ... and loaded by the compute warps (256 arrivals)
@@ -171,7 +182,7 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
   if (threadIdx.x == 0) {
     tc::mbar_init(kv_full, 1);
     for (int b = 0; b < QST; ++b) {
-      tc::mbar_init(q_full + b, 1);
+      tc::mbar_init(q_full + b, kRowStage ? 2 : 1);  // TMA bytes (+ the row-term stores)
       tc::mbar_init(q_empty + b, 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -206,31 +217,68 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0 && n_iter > 0) {
-      tc::prefetch_tmap(&tm_q);
-      tc::prefetch_tmap(&tm_do);
-      tc::mbar_expect_tx(kv_full, 2 * L::kKV);
-      for (int cb = 0; cb < HD / 64; ++cb) {
-        tc::tma_load_3d(smem + L::oK + cb * BK * 128, &tm_k, kv_full, cb * 64, k0, bh);
-        tc::tma_load_3d(smem + L::oV + cb * BK * 128, &tm_v, kv_full, cb * 64, k0, bh);
+    // Lane 0 issues the TMA copies; the whole warp stages each tile's row
+    // terms in shared memory, where the compute warps read them as
+    // broadcast vector loads (instead of one shuffle per query and term).
+    if (n_iter > 0) {
+      if (lane == 0) {
+        tc::prefetch_tmap(&tm_q);
+        tc::prefetch_tmap(&tm_do);
+        tc::mbar_expect_tx(kv_full, 2 * L::kKV);
+        for (int cb = 0; cb < HD / 64; ++cb) {
+          tc::tma_load_3d(smem + L::oK + cb * BK * 128, &tm_k, kv_full, cb * 64, k0, bh);
+          tc::tma_load_3d(smem + L::oV + cb * BK * 128, &tm_v, kv_full, cb * 64, k0, bh);
+        }
       }
+      const size_t row_base = (size_t)bh * Tq;
+      // row terms of tile t, loaded one tile ahead so their latency never
+      // delays a TMA issue; negated, so they enter paired adds / fmas
+      // directly (rows past the end: P = exp2(-inf) = 0)
+      float2 rv[2];
+      auto load_rows = [&](int t) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int q = tile_of(t) * BQ + h * 32 + lane;
+          rv[h] = q < Tq ? make_float2(-__ldg(lse + row_base + q) * 1.4426950408889634f,
+                                       -__ldg(z + row_base + q))
+                         : make_float2(-INFINITY, 0.f);
+        }
+      };
+      if (kRowStage) load_rows(0);
       int issued = 0;
       for (int t = 0; t < n_iter; ++t) {
+        // without staged row terms only lane 0 runs this loop
+        if (!kRowStage && lane != 0) break;
         const int st = t % QST;
-        if (t >= QST && !tc::mbar_wait(q_empty + st, ((t / QST) - 1) & 1, abort)) break;
+        bool ok = true;
+        if (lane == 0 && t >= QST) ok = tc::mbar_wait(q_empty + st, ((t / QST) - 1) & 1, abort);
+        if (kRowStage) ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
         const int q0 = tile_of(t) * BQ;
-        tc::mbar_expect_tx(q_full + st, 2 * L::kQ);
-        for (int cb = 0; cb < HD / 64; ++cb) {
-          tc::tma_load_3d(smem + L::oQ + st * L::kQ + cb * BQ * 128, &tm_q, q_full + st,
-                          cb * 64, q0, bh);
-          tc::tma_load_3d(smem + L::oDO + st * L::kQ + cb * BQ * 128, &tm_do, q_full + st,
-                          cb * 64, q0, bh);
+        if (lane == 0) {
+          tc::mbar_expect_tx(q_full + st, 2 * L::kQ);
+          for (int cb = 0; cb < HD / 64; ++cb) {
+            tc::tma_load_3d(smem + L::oQ + st * L::kQ + cb * BQ * 128, &tm_q, q_full + st,
+                            cb * 64, q0, bh);
+            tc::tma_load_3d(smem + L::oDO + st * L::kQ + cb * BQ * 128, &tm_do, q_full + st,
+                            cb * 64, q0, bh);
+          }
+        }
+        if (kRowStage) {
+          float2* rt = reinterpret_cast<float2*>(smem + L::oRow + st * L::kRow);
+          rt[lane] = rv[0];
+          rt[32 + lane] = rv[1];
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive(q_full + st);
+          if (t + 1 < n_iter) load_rows(t + 1);
         }
         issued = t + 1;
       }
-      tc::mbar_wait_drain(kv_full, 0);
-      for (int t = issued > QST ? issued - QST : 0; t < issued; ++t)
-        tc::mbar_wait_drain(q_full + t % QST, (t / QST) & 1);
+      if (lane == 0) {
+        tc::mbar_wait_drain(kv_full, 0);
+        for (int t = issued > QST ? issued - QST : 0; t < issued; ++t)
+          tc::mbar_wait_drain(q_full + t % QST, (t / QST) & 1);
+      }
     }
   } else if (warp == 1 || warp == 2) {
     // ------------------------------------------------------------ MMA issuers
@@ -368,12 +416,18 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
     for (int t = 0; ok && t < n_iter; ++t) {
       const int b = t & 1;
       const int q0 = tile_of(t) * BQ;
-      // Row statistics of this group's 32 queries: one load per lane, then
-      // broadcast by shuffles.
-      const int ql = q0 + grp * 32 + lane;
-      // negated, so the row terms enter paired adds / fmas directly
-      const float my_l = ql < Tq ? -__ldg(lse + row_base + ql) * 1.4426950408889634f : -INFINITY;
-      const float my_z = ql < Tq ? -__ldg(z + row_base + ql) : 0.f;
+      // Row terms of this group's 32 queries: staged by the producer warp,
+      // or one load per lane broadcast by shuffles below.
+      const uint32_t rows_at = tc::smem_u32(smem + L::oRow + (t % QST) * L::kRow) + grp * 32 * 8;
+      float my_l = 0.f, my_z = 0.f;
+      if (kRowStage) {
+        if (!wait(q_full + t % QST, (t / QST) & 1)) { ok = false; break; }
+      } else {
+        const int ql = q0 + grp * 32 + lane;
+        // negated, so the row terms enter paired adds / fmas directly
+        my_l = ql < Tq ? -__ldg(lse + row_base + ql) * 1.4426950408889634f : -INFINITY;
+        my_z = ql < Tq ? -__ldg(z + row_base + ql) : 0.f;
+      }
       if (!wait(s_full, t & 1)) { ok = false; break; }
       tc::tc_fence_after();
       float s[32], dp[32];
@@ -397,10 +451,17 @@ bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       // two columns at a time on paired fp32 instructions
 #pragma unroll
       for (int e = 0; e < 32; e += 2) {
-        const float nl0 = __shfl_sync(0xffffffffu, my_l, e);
-        const float nl1 = __shfl_sync(0xffffffffu, my_l, e + 1);
-        const float nz0 = __shfl_sync(0xffffffffu, my_z, e);
-        const float nz1 = __shfl_sync(0xffffffffu, my_z, e + 1);
+        float nl0, nl1, nz0, nz1;
+        if (kRowStage) {
+          // {-l, -z} of queries e and e+1: one broadcast 16-byte load
+          const float4 rr = tc::ld_shared_f4(rows_at + e * 8);
+          nl0 = rr.x; nz0 = rr.y; nl1 = rr.z; nz1 = rr.w;
+        } else {
+          nl0 = __shfl_sync(0xffffffffu, my_l, e);
+          nl1 = __shfl_sync(0xffffffffu, my_l, e + 1);
+          nz0 = __shfl_sync(0xffffffffu, my_z, e);
+          nz1 = __shfl_sync(0xffffffffu, my_z, e + 1);
+        }
         float x0, x1, g0, g1;
         tc::fma2(x0, x1, s[e], s[e + 1], scale_log2, scale_log2, nl0, nl1);
         float p0 = tc::ex2(x0), p1 = tc::ex2(x1);  // rows past the end: -inf -> 0

@@ -15,10 +15,11 @@
 // TMEM: S^T [0,64), Sd^T [64,128), dP^T [128,192), dPd^T [192,256),
 // hV [256, 256+D), hK [256+D, 256+2D), pair hQ [384, 448) for D = 64.
 // Warp roles: 0 TMA, 1 issues the S-group products (and owns TMEM), 2
-// issues hK, hV and hQ, 3 idle, 4..11 compute, 12..15 hQ flush.  With the two groups
-// on separate threads the next tile's S-group (D = 64) runs on the tensor
-// core while the CUDA cores still work on the current tile; for D = 128 the
-// S-group waits for hQ^T to leave the S^T columns.
+// issues hK, hV and hQ, 3 stages the row terms, 4..11 compute, 12..15 hQ
+// flush.  With the two groups on separate threads the next tile's S-group
+// (D = 64) runs on the tensor core while the CUDA cores still work on the
+// current tile; for D = 128 the S-group waits for hQ^T to leave the S^T
+// columns.
 #pragma once
 
 #include "sdpa_tc_bwd.cuh"
@@ -57,7 +58,13 @@ struct Cfg {
   // [128 q][32 d] for the bulk tensor reduction (D = 64 only)
   static constexpr int oStage = oDSd + NB * kP;
   static constexpr int kStage = HD == 64 ? 32768 : 0;
-  static constexpr int oBar = oStage + kStage;
+  // per Q/tQ/W stage, row terms of the tile's 64 queries staged by warp 3:
+  // {-LSE*log2(e), -z} (D = 64; c and zdot stay on shuffles: the shared
+  // memory has room for no more) or {-LSE*log2(e), -c, -z, -zdot} (D = 128)
+  static constexpr int NTERM = HD == 64 ? 2 : 4;
+  static constexpr int kRow = BQ * NTERM * 4;
+  static constexpr int oRow = oStage + kStage;
+  static constexpr int oBar = oRow + ST * kRow;
   // kv_full, q_full[3], q_empty[3], s_full, s_read, p_full, mma2_done[2],
   // hq_free, drain[2], stage_free, stage_full
   static constexpr int nBar = 17;
@@ -78,6 +85,10 @@ hvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
            float scale_log2, float* __restrict__ hkv_acc, int n_split) {
   using C = Cfg<HD>;
   constexpr bool kPair = (HD == 64);
+  // Row terms staged in shared memory by warp 3 (see there): measured
+  // +4-7 % non-causal; causal grids (many short CTAs) measured 0-5 % slower
+  // with it, so they keep the shuffles.
+  constexpr bool kRowStage = !CAUSAL;
   constexpr int ST = C::ST;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -108,7 +119,7 @@ hvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
   if (threadIdx.x == 0) {
     tc::mbar_init(kv_full, 1);
     for (int b = 0; b < 3; ++b) {
-      tc::mbar_init(q_full + b, 1);
+      tc::mbar_init(q_full + b, kRowStage ? 2 : 1);  // TMA bytes (+ warp 3's row terms)
       tc::mbar_init(q_empty + b, 1);
     }
     for (int b = 0; b < 2; ++b) tc::mbar_init(mma2_done + b, 1);
@@ -266,7 +277,45 @@ hvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       }
     }
   } else if (warp < kFirstCompute) {
-    // warp 3: no role (it completes the control warpgroup)
+    // ------------------------------------------------------------ row terms
+    // Warp 3 stages each tile's per-query row terms in shared memory (one
+    // tile ahead of their use), where the compute warps read them as
+    // broadcast vector loads instead of one shuffle per query and term.
+    if (kRowStage && n_iter > 0) {
+      const size_t row_base = (size_t)bh * Tq;
+      float rv[2][C::NTERM];
+      auto load_rows = [&](int t) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int q = (i_begin + t) * BQ + h * 32 + lane;
+          const bool in = q < Tq;
+          // negated, so they enter paired adds / fmas directly
+          rv[h][0] = in ? -__ldg(lse + row_base + q) * 1.4426950408889634f : -INFINITY;
+          if constexpr (C::NTERM == 2) {
+            rv[h][1] = in ? -__ldg(stats + n_rows_total + row_base + q) : 0.f;
+          } else {
+            rv[h][1] = in ? -__ldg(stats + row_base + q) : 0.f;
+            rv[h][2] = in ? -__ldg(stats + n_rows_total + row_base + q) : 0.f;
+            rv[h][3] = in ? -__ldg(stats + 2 * n_rows_total + row_base + q) : 0.f;
+          }
+        }
+      };
+      load_rows(0);
+      for (int t = 0; t < n_iter; ++t) {
+        const int st = t % ST;
+        bool ok = true;
+        if (lane == 0 && t >= ST) ok = tc::mbar_wait(q_empty + st, ((t / ST) - 1) & 1, abort);
+        if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+        float* rt = reinterpret_cast<float*>(smem + C::oRow + st * C::kRow);
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int i = 0; i < C::NTERM; ++i) rt[(h * 32 + lane) * C::NTERM + i] = rv[h][i];
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(q_full + st);
+        if (t + 1 < n_iter) load_rows(t + 1);
+      }
+    }
   } else if (warp < kFirstCompute + NCOMPUTE / 32) {
     // ------------------------------------------------------------ compute
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegCompute));
@@ -287,11 +336,23 @@ hvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
       const int q0 = (i_begin + t) * BQ;
       const int ql = q0 + grp * 32 + lane;
       const bool qin = ql < Tq;
-      // negated, so the row terms enter paired adds / fmas directly
-      const float my_l = qin ? -__ldg(lse + row_base + ql) * 1.4426950408889634f : -INFINITY;
-      const float my_c = qin ? -__ldg(stats + row_base + ql) : 0.f;
-      const float my_z = qin ? -__ldg(stats + n_rows_total + row_base + ql) : 0.f;
-      const float my_zd = qin ? -__ldg(stats + 2 * n_rows_total + row_base + ql) : 0.f;
+      // Row terms of this group's 32 queries: staged in shared memory by
+      // warp 3 (all four for D = 128; LSE and z for D = 64), the others one
+      // load per lane broadcast by shuffles.  Negated, so they enter paired
+      // adds / fmas directly.
+      const uint32_t rows_at =
+          tc::smem_u32(smem + C::oRow + (t % ST) * C::kRow) + grp * 32 * C::NTERM * 4;
+      float my_l = 0.f, my_c = 0.f, my_z = 0.f, my_zd = 0.f;
+      if (kRowStage) {
+        if (!wait(q_full + t % ST, (t / ST) & 1)) { ok = false; break; }
+      } else {
+        my_l = qin ? -__ldg(lse + row_base + ql) * 1.4426950408889634f : -INFINITY;
+        my_z = qin ? -__ldg(stats + n_rows_total + row_base + ql) : 0.f;
+      }
+      if (!kRowStage || C::NTERM == 2) {
+        my_c = qin ? -__ldg(stats + row_base + ql) : 0.f;
+        my_zd = qin ? -__ldg(stats + 2 * n_rows_total + row_base + ql) : 0.f;
+      }
       if (!wait(s_full, t & 1)) { ok = false; break; }
       tc::tc_fence_after();
       float sv[32], sd[32], dp[32], dpd[32];
@@ -309,12 +370,26 @@ hvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
 #pragma unroll
       for (int e = 0; e < 32; e += 2) {
         float nl[2], nc[2], nz[2], nzd[2];
+        if (kRowStage && C::NTERM == 4) {
 #pragma unroll
-        for (int i = 0; i < 2; ++i) {
-          nl[i] = __shfl_sync(0xffffffffu, my_l, e + i);
-          nc[i] = __shfl_sync(0xffffffffu, my_c, e + i);
-          nz[i] = __shfl_sync(0xffffffffu, my_z, e + i);
-          nzd[i] = __shfl_sync(0xffffffffu, my_zd, e + i);
+          for (int i = 0; i < 2; ++i) {
+            const float4 rr = tc::ld_shared_f4(rows_at + (e + i) * 16);
+            nl[i] = rr.x; nc[i] = rr.y; nz[i] = rr.z; nzd[i] = rr.w;
+          }
+        } else {
+          if (kRowStage) {
+            const float4 rr = tc::ld_shared_f4(rows_at + e * 8);  // {l, z} of e, e+1
+            nl[0] = rr.x; nz[0] = rr.y; nl[1] = rr.z; nz[1] = rr.w;
+          }
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            if (!kRowStage) {
+              nl[i] = __shfl_sync(0xffffffffu, my_l, e + i);
+              nz[i] = __shfl_sync(0xffffffffu, my_z, e + i);
+            }
+            nc[i] = __shfl_sync(0xffffffffu, my_c, e + i);
+            nzd[i] = __shfl_sync(0xffffffffu, my_zd, e + i);
+          }
         }
         float x0, x1, pd0, pd1, g0, g1, h0, h1;
         tc::fma2(x0, x1, sv[e], sv[e + 1], scale_log2, scale_log2, nl[0], nl[1]);
