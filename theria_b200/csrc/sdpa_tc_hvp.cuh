@@ -35,12 +35,31 @@ constexpr int NCOMPUTE = 256, NDQ = 128;
 // 32-column rows of scores at once.
 constexpr int NTHREADS = 128 + NCOMPUTE + NDQ;
 constexpr int kFirstCompute = 4;
-constexpr int kRegCtl = 112, kRegCompute = 144, kRegFlush = 112;
-// a warp's launch allocation is the largest multiple of 8 registers that
-// fits NTHREADS threads in 64K; a split above it would wait forever
-static_assert((kRegCtl + 2 * kRegCompute + kRegFlush) * 128 <=
-                  (65536 / NTHREADS) / 8 * 8 * NTHREADS,
-              "register split exceeds the launch allocation");
+// Per head dim (control, compute, flush), registers per thread; measured
+// at configs[2] and B1 H32 N4096: D = 64 gains 1-3 % from a leaner control
+// and flush group, D = 128 (whose control and flush code needs the room)
+// does not.
+#ifndef THERIA_HVP64_RC
+#define THERIA_HVP64_RC 96
+#define THERIA_HVP64_RM 160
+#define THERIA_HVP64_RF 96
+#endif
+#ifndef THERIA_HVP128_RC
+#define THERIA_HVP128_RC 112
+#define THERIA_HVP128_RM 144
+#define THERIA_HVP128_RF 112
+#endif
+template <int HD>
+struct RegSplit {
+  static constexpr int ctl = HD == 64 ? THERIA_HVP64_RC : THERIA_HVP128_RC;
+  static constexpr int compute = HD == 64 ? THERIA_HVP64_RM : THERIA_HVP128_RM;
+  static constexpr int flush = HD == 64 ? THERIA_HVP64_RF : THERIA_HVP128_RF;
+  static constexpr int total = ctl + 2 * compute + flush;
+  // a warp's launch allocation is the largest multiple of 8 registers that
+  // fits NTHREADS threads in 64K; a split above it would wait forever
+  static_assert(total * 128 <= (65536 / NTHREADS) / 8 * 8 * NTHREADS,
+                "register split exceeds the launch allocation");
+};
 
 template <int HD>
 struct Cfg {
@@ -142,7 +161,7 @@ hvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
   const uint32_t t_hv = tmem + 256, t_hk = tmem + 256 + HD, t_hqp = tmem + 384;
 
   if (warp < kFirstCompute)
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegCtl));
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(RegSplit<HD>::ctl));
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0 && n_iter > 0) {
@@ -318,7 +337,7 @@ hvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
     }
   } else if (warp < kFirstCompute + NCOMPUTE / 32) {
     // ------------------------------------------------------------ compute
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegCompute));
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(RegSplit<HD>::compute));
     const int grp = (warp - kFirstCompute) >> 2;
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;  // TMEM lane = key row
@@ -490,7 +509,7 @@ hvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUt
     }
   } else {
     // ------------------------------------------------------------ hQ flush
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegFlush));
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(RegSplit<HD>::flush));
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;

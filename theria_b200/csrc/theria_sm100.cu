@@ -483,7 +483,7 @@ int tc_hvp_launch(const CUtensorMap* m, const float* lse, const float* stats, fl
   using C = tchvp::Cfg<HD>;
   auto kern = tchvp::hvp_kernel<T, HD, CAUSAL>;
   static const bool regs_ok = regs_cover_split(
-      kern, tchvp::NTHREADS, tchvp::kRegCtl + 2 * tchvp::kRegCompute + tchvp::kRegFlush);
+      kern, tchvp::NTHREADS, tchvp::RegSplit<HD>::total);
   if (!regs_ok) return THERIA_ERR_LAUNCH;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kAlloc);
   dim3 grid((unsigned)((s.M + tchvp::BK - 1) / tchvp::BK), (unsigned)(s.B * s.H), split);
