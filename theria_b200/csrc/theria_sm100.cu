@@ -302,7 +302,7 @@ int tc_fwd_launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMa
   dim3 grid((unsigned)((s.T + tcfwd::NQT * tcfwd::BM - 1) / (tcfwd::NQT * tcfwd::BM)),
             (unsigned)(s.B * s.H));
   if (CAUSAL) grid = dim3(grid.y, grid.x);  // head index in x: longest tiles first
-  kern<<<grid, tcfwd::NTHREADS, smem, st>>>(mq, mk, mv, o, out_f32, lse, (int)s.T, (int)s.M,
+  kern<<<grid, tcfwd::Cfg<HD>::kThreads, smem, st>>>(mq, mk, mv, o, out_f32, lse, (int)s.T, (int)s.M,
                                             s.scale * 1.4426950408889634f);
   return launch_status();
 }
