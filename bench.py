@@ -633,7 +633,7 @@ def profile_maml_step(tasks=4, top=25):
 
 def profile_case(case):
     """A few launches of one operator at a size ncu can capture in minutes
-    (inputs still larger than L2): --profile-case fwdbwd|jvp|hvp, or
+    (inputs still larger than L2): --profile-case fwdbwd|fwd64|jvp|hvp, or
     maml_heads: forward + HVP of 3,200 fp32 MAML heads [800, 4, 64, 16]
     (the whole-head kernels); maml_step: kernel list of one meta-step."""
     from theria_b200.attention import ops
@@ -642,6 +642,8 @@ def profile_case(case):
         return profile_maml_step()
     if case == "maml_heads":
         shape = (800, 4, 64, 16)
+    elif case == "fwd64":
+        shape = (1, 32, 8192, 64)
     elif case == "fwdbwd":
         shape = (1, 16, 4096, 128)
     else:
@@ -655,7 +657,7 @@ def profile_case(case):
             ops.backward(q, k, v, w, lse, o=o)
         elif case == "jvp":
             ops.jvp(q, k, v, tq, tk, tv, lse)
-        else:
+        elif case != "fwd64":
             ops.hvp(q, k, v, w, lse, tq, tk, tv)
     torch.cuda.synchronize()
     print(json.dumps({"profile_case": case, "shape": list(shape), "ok": True}))
@@ -673,7 +675,8 @@ def main():
                     help="run every configs[4] sweep point (default: D 64/128 x N 4096/16384)")
     ap.add_argument("--cpu-budget", type=float, default=12.0,
                     help="seconds of CPU work for the cpu_baseline sample")
-    ap.add_argument("--profile-case", choices=["fwdbwd", "jvp", "hvp", "maml_heads", "maml_step"],
+    ap.add_argument("--profile-case",
+                    choices=["fwdbwd", "fwd64", "jvp", "hvp", "maml_heads", "maml_step"],
                     default=None,
                     help="run a few launches of one operator for ncu, print no bench line")
     args = ap.parse_args()
