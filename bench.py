@@ -633,7 +633,7 @@ def profile_maml_step(tasks=4, top=25):
 
 def profile_case(case):
     """A few launches of one operator at a size ncu can capture in minutes
-    (inputs still larger than L2): --profile-case fwdbwd|fwd64|jvp|hvp, or
+    (inputs still larger than L2): --profile-case fwdbwd|fwd64|bwd64|jvp|hvp, or
     maml_heads: forward + HVP of 3,200 fp32 MAML heads [800, 4, 64, 16]
     (the whole-head kernels); maml_step: kernel list of one meta-step."""
     from theria_b200.attention import ops
@@ -644,6 +644,8 @@ def profile_case(case):
         shape = (800, 4, 64, 16)
     elif case == "fwd64":
         shape = (1, 32, 8192, 64)
+    elif case == "bwd64":
+        shape = (1, 32, 4096, 64)
     elif case == "fwdbwd":
         shape = (1, 16, 4096, 128)
     else:
@@ -653,7 +655,7 @@ def profile_case(case):
     q, k, v, w, tq, tk, tv = (randn(shape, gen, dt, "cuda") for _ in range(7))
     for _ in range(3):
         o, lse = ops.forward(q, k, v)
-        if case == "fwdbwd":
+        if case in ("fwdbwd", "bwd64"):
             ops.backward(q, k, v, w, lse, o=o)
         elif case == "jvp":
             ops.jvp(q, k, v, tq, tk, tv, lse)
@@ -676,7 +678,7 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=12.0,
                     help="seconds of CPU work for the cpu_baseline sample")
     ap.add_argument("--profile-case",
-                    choices=["fwdbwd", "fwd64", "jvp", "hvp", "maml_heads", "maml_step"],
+                    choices=["fwdbwd", "fwd64", "bwd64", "jvp", "hvp", "maml_heads", "maml_step"],
                     default=None,
                     help="run a few launches of one operator for ncu, print no bench line")
     args = ap.parse_args()
