@@ -82,6 +82,8 @@ SHAPES = [
     (1, 1, 200, 200, 48),  # head dim off the tensor-core list
     (1, 2, 384, 640, 64),  # several key/query tiles, T < M
     (1, 2, 640, 384, 128), # T > M: keys past every causal query row
+    (1, 2, 190, 200, 128), # ragged key tile ending in its second 64-column half
+    (1, 1, 300, 230, 64),  # ragged key tile, T > M, D = 64
     (1, 2, 20, 50, 16),    # whole-head kernels, T != M
     (2, 1, 64, 33, 20),    # whole-head kernels, odd head dim
 ]
